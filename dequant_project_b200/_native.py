@@ -1,0 +1,62 @@
+"""ctypes binding of libdequant_b200.so, the library's C ABI (include/dequant_b200.h).
+
+The shared library is built in-tree by ``python -m dequant_project_b200.build``.
+There is no fallback: if the library is missing or fails to load, every
+operation raises, so a GPU run can never silently take a CPU or eager-PyTorch
+path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libdequant_b200.so"
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH.name} is not built. Build it once with:\n"
+            "    python -m dequant_project_b200.build\n"
+            "(or call __graft_entry__.build()); re-run after any change under csrc/.")
+    h = ctypes.CDLL(str(LIB_PATH))
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    h.dqg_last_error.restype = ctypes.c_char_p
+    h.dqg_last_error.argtypes = []
+    h.dqg_version.restype = i32
+    h.dqg_add_one.restype = i32
+    h.dqg_add_one.argtypes = [vp, vp, i64, vp]
+    h.dqg_gemv.restype = i32
+    h.dqg_gemv.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp]
+    h.dqg_dequantize.restype = i32
+    h.dqg_dequantize.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, vp]
+    h.dqg_device_status.restype = i32
+    h.dqg_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
+    _lib = h
+    return _lib
+
+
+# Every symbol the C header declares; tests check the library exports them all.
+EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_dequantize",
+            "dqg_device_status")
+
+
+def check(rc: int) -> None:
+    """Turn a non-zero dqg_status into RuntimeError with the library's message."""
+    if rc != 0:
+        msg = lib().dqg_last_error().decode(errors="replace")
+        raise RuntimeError(msg or f"dequant_b200 call failed with status {rc}")
+
+
+def device_status(device: int, reset: bool = False) -> int:
+    """Read the device-side status word (bit 0: a kernel gave up a bounded wait)."""
+    v = ctypes.c_uint32(0)
+    check(lib().dqg_device_status(int(device), ctypes.byref(v), int(reset)))
+    return v.value

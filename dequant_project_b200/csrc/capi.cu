@@ -1,0 +1,232 @@
+// extern "C" entry points of libdequant_b200.so (declared in
+// include/dequant_b200.h). Argument validation follows the reference
+// extension's TORCH_CHECKs (kernels/dequant_gemv.cu:230-283 check_weight,
+// :310-317 dequantize, :339-361 gemv, kernels/smoke.cu:15-25 add_one) with the
+// same messages, adapted to raw pointers: dtype/contiguity checks become
+// pointer-kind and alignment checks. Nothing here allocates or synchronises.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <cuda_runtime.h>
+
+#include "../../include/dequant_b200.h"
+#include "gemv.h"
+
+namespace {
+
+thread_local char g_msg[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DQG_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int ok() {
+  g_msg[0] = '\0';
+  return DQG_OK;
+}
+
+// A pointer the kernels may dereference: device or managed memory of `dev`.
+int check_device_ptr(const void* p, int dev, const char* name) {
+  if (p == nullptr) return fail(DQG_ERR_INVALID, "%s must not be null", name);
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error this query may leave
+    return fail(DQG_ERR_INVALID, "%s must be a CUDA tensor (%s)", name, cudaGetErrorString(e));
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return fail(DQG_ERR_INVALID, "%s must be a CUDA tensor", name);
+  if (attr.type == cudaMemoryTypeDevice && attr.device != dev)
+    return fail(DQG_ERR_INVALID, "%s and qweight must be on the same device", name);
+  return DQG_OK;
+}
+
+int sm_count(int dev) {
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev >= 0 && dev < 64) cache[dev] = v;
+  return v;
+}
+
+// check_weight (kernels/dequant_gemv.cu:230-283), scalar half: sizes, format
+// and alignment. Runs before any CUDA call.
+int check_weight_args(const int32_t* qweight, const void* scales, const void* zeros, int64_t N,
+                      int64_t K, int64_t bits, int64_t group_size, int symmetric) {
+  if (bits != 2 && bits != 4 && bits != 8)
+    return fail(DQG_ERR_INVALID, "bits must be 2, 4 or 8, got %lld", (long long)bits);
+  if (group_size <= 0)
+    return fail(DQG_ERR_INVALID, "group_size must be positive, got %lld", (long long)group_size);
+  if (K <= 0 || K % group_size != 0)
+    return fail(DQG_ERR_INVALID, "K=%lld is not divisible by group_size=%lld", (long long)K,
+                (long long)group_size);
+  if (N <= 0)
+    return fail(DQG_ERR_INVALID, "qweight must have at least one row, got N=%lld", (long long)N);
+  if (K % (32 / bits) != 0)
+    return fail(DQG_ERR_INVALID, "K=%lld is not a whole number of %lld-code words",
+                (long long)K, (long long)(32 / bits));
+  if (N > INT32_MAX || K > (1 << 24))
+    return fail(DQG_ERR_UNSUPPORTED, "N=%lld, K=%lld exceed the supported sizes", (long long)N,
+                (long long)K);
+  if ((zeros != nullptr) == (symmetric != 0))
+    return fail(DQG_ERR_INVALID, symmetric ? "symmetric=true takes no zeros"
+                                           : "symmetric=false requires zeros");
+  if (qweight == nullptr) return fail(DQG_ERR_INVALID, "qweight must not be null");
+  if (scales == nullptr) return fail(DQG_ERR_INVALID, "scales must not be null");
+  if (reinterpret_cast<uintptr_t>(qweight) % 4)
+    return fail(DQG_ERR_INVALID, "qweight must be 4-byte aligned");
+  if (reinterpret_cast<uintptr_t>(scales) % 2)
+    return fail(DQG_ERR_INVALID, "scales must be 2-byte aligned");
+  if (zeros && reinterpret_cast<uintptr_t>(zeros) % 2)
+    return fail(DQG_ERR_INVALID, "zeros must be 2-byte aligned");
+  return DQG_OK;
+}
+
+// check_weight, device half: every pointer is device (or managed) memory of
+// the current device.
+int check_weight_ptrs(const int32_t* qweight, const void* scales, const void* zeros, int dev) {
+  int rc = check_device_ptr(qweight, dev, "qweight");
+  if (rc) return rc;
+  rc = check_device_ptr(scales, dev, "scales");
+  if (rc) return rc;
+  if (zeros) rc = check_device_ptr(zeros, dev, "zeros");
+  return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* dqg_last_error(void) { return g_msg; }
+
+int dqg_version(void) { return 100; }
+
+int dqg_add_one(const float* x, float* out, int64_t n, void* stream) {
+  if (n < 0) return fail(DQG_ERR_INVALID, "n must be non-negative");
+  if (n == 0) return ok();
+  if (x == nullptr || out == nullptr) return fail(DQG_ERR_INVALID, "x and out must not be null");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int rc = check_device_ptr(x, dev, "x");
+  if (rc) return rc;
+  rc = check_device_ptr(out, dev, "out");
+  if (rc) return rc;
+  e = dqg::launch_add_one(x, out, n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add_one launch");
+  return ok();
+}
+
+int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+             void* y, int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+             int symmetric, int interleaved, void* stream) {
+  if (M < 1 || M > dqg::kMaxM)
+    return fail(DQG_ERR_INVALID,
+                "gemv handles 1 <= M <= %d, got M=%lld; use the dequantize + F.linear fallback",
+                dqg::kMaxM, (long long)M);
+  int rc = check_weight_args(qweight, scales, zeros, N, K, bits, group_size, symmetric);
+  if (rc) return rc;
+  if (x == nullptr) return fail(DQG_ERR_INVALID, "x must not be null");
+  if (y == nullptr) return fail(DQG_ERR_INVALID, "y must not be null");
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail(DQG_ERR_INVALID, "x must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(qweight) % 16)
+    return fail(DQG_ERR_INVALID, "qweight must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(y) % 2) return fail(DQG_ERR_INVALID, "y must be 2-byte aligned");
+  const int64_t cpl = 128 / bits;
+  if (group_size % cpl != 0)
+    return fail(DQG_ERR_INVALID,
+                "group_size=%lld must be a multiple of %lld (the codes one lane loads per uint4) "
+                "at %lld bits; this excludes INT2 with group_size 32",
+                (long long)group_size, (long long)cpl, (long long)bits);
+  const int wpl = dqg::gemv_words_per_lane(static_cast<int>(bits), static_cast<int>(group_size),
+                                           static_cast<int>(K));
+  if (wpl == 0 || K / (4 * wpl * (32 / bits)) >= 65536)
+    return fail(DQG_ERR_UNSUPPORTED, "K=%lld is too large for the GEMV path", (long long)K);
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  rc = check_weight_ptrs(qweight, scales, zeros, dev);
+  if (rc) return rc;
+  rc = check_device_ptr(x, dev, "x");
+  if (rc) return rc;
+  rc = check_device_ptr(y, dev, "y");
+  if (rc) return rc;
+
+  dqg::GemvPlan plan;
+  if (!dqg::plan_gemv(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                      static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev), &plan))
+    return fail(DQG_ERR_UNSUPPORTED, "no shared-memory plan for M=%lld K=%lld bits=%lld group=%lld",
+                (long long)M, (long long)K, (long long)bits, (long long)group_size);
+  dqg::GemvArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.qweight = reinterpret_cast<const uint32_t*>(qweight);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.zeros = static_cast<const uint16_t*>(zeros);
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.bits = static_cast<int>(bits);
+  a.group_size = static_cast<int>(group_size);
+  a.symmetric = symmetric != 0;
+  a.interleaved = interleaved != 0;
+  e = dqg::launch_gemv(a, plan, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  return ok();
+}
+
+int dqg_dequantize(const int32_t* qweight, const void* scales, const void* zeros, void* out,
+                   int64_t N, int64_t K, int64_t bits, int64_t group_size, int symmetric,
+                   int interleaved, void* stream) {
+  int rc = check_weight_args(qweight, scales, zeros, N, K, bits, group_size, symmetric);
+  if (rc) return rc;
+  const int64_t per_pack = 32 / bits;
+  if (group_size % per_pack != 0)
+    return fail(DQG_ERR_INVALID,
+                "group_size=%lld must be a multiple of %lld values per uint32 word at %lld bits",
+                (long long)group_size, (long long)per_pack, (long long)bits);
+  if (out == nullptr) return fail(DQG_ERR_INVALID, "out must not be null");
+  if (reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(DQG_ERR_INVALID, "out must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  rc = check_weight_ptrs(qweight, scales, zeros, dev);
+  if (rc) return rc;
+  rc = check_device_ptr(out, dev, "out");
+  if (rc) return rc;
+  dqg::DequantArgs a;
+  a.qweight = reinterpret_cast<const uint32_t*>(qweight);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.zeros = static_cast<const uint16_t*>(zeros);
+  a.out = static_cast<uint16_t*>(out);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.bits = static_cast<int>(bits);
+  a.group_size = static_cast<int>(group_size);
+  a.symmetric = symmetric != 0;
+  a.interleaved = interleaved != 0;
+  e = dqg::launch_dequantize(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dequantize launch");
+  return ok();
+}
+
+int dqg_device_status(int device, uint32_t* status, int reset) {
+  if (status == nullptr) return fail(DQG_ERR_INVALID, "status must not be null");
+  cudaError_t e = dqg::read_device_status(device, status, reset != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  return ok();
+}
+
+}  // extern "C"

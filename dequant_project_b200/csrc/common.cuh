@@ -1,0 +1,162 @@
+// Device-side building blocks shared by the sm_100a kernels of this library:
+// mbarrier pipeline primitives, untiled bulk copies global->shared, named
+// barriers, a bounded wait that reports instead of hanging, and small
+// integer helpers. Hand-written inline PTX; no library code.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace dqg {
+
+// Bits of the device status word g_status. A kernel that
+// gives up a bounded wait ORs one of these in and returns instead of hanging;
+// the host reads it with dqg_device_status().
+enum : uint32_t {
+  kStatusWaitTimeout = 1u << 0,   // an mbarrier wait ran past its time limit
+};
+
+// One status word per translation unit that includes this header (internal
+// linkage; the library is built without relocatable device code). The unit
+// that launches waiting kernels also provides the host-side reader.
+static __device__ uint32_t g_status = 0;
+
+// Upper bound on any single mbarrier wait (nanoseconds of %globaltimer). A
+// healthy stage wait is microseconds; this is five orders of magnitude above.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+// Make mbarrier.init visible to the async proxy (bulk copies) and other threads.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete. Bounded: after
+// kWaitLimitNs the wait gives up, flags kStatusWaitTimeout in g_status and
+// returns false so that the caller can leave its loop and the kernel ends.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      atomicOr(&g_status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// mbar_wait taken by all 32 lanes of a warp with a warp-uniform outcome, so
+// that a timed-out warp leaves its loop as a whole (no lane is left behind in
+// a later __syncwarp or vote).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  const bool ok = mbar_wait(bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing as
+// transaction bytes on `bar`. dst, src and bytes must be multiples of 16.
+// No multicast: the source is always this GPU's own memory.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 policies for the bulk copies: packed weights are streamed exactly once
+// per call (evict first); activations are re-read by every CTA (evict last).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Named barrier among a subset of warps (id 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// d = (a & b) | c, one LOP3.
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Select two fp16 halves from {lo: a, hi: b} by byte selector (PRMT).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// floor(n / d) for n < 2^16 and 1 <= d < 2^16, with magic = ceil(2^32 / d)
+// (magic == 0 encodes d == 1). Exact in that range: the error of the
+// reciprocal is below n / 2^32 < 1 / d.
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t magic) {
+  return magic ? __umulhi(n, magic) : n;
+}
+
+}  // namespace dqg

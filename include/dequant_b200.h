@@ -1,0 +1,95 @@
+/*
+ * dequant_b200 -- C ABI of the B200 (sm_100a) packed low-bit dequant + GEMV
+ * library, libdequant_b200.so.
+ *
+ * Drop-in boundary for the `dequant_cuda` torch extension of
+ * KrishnaI2424/Dequant_Project (kernels/dequant_cuda.h, kernels/bindings.cpp):
+ * the same three operations with the same argument meaning and the same
+ * validation rules, expressed with plain device pointers, sizes and a CUDA
+ * stream instead of torch tensors. No torch types cross this boundary.
+ *
+ * Conventions
+ *   - All data pointers are CUDA device pointers on the stream's device. fp16
+ *     tensors are passed as `const void *` (IEEE binary16, little endian).
+ *   - The packed format is the reference packer's (dequant/packer.py:7-29):
+ *     qweight is int32 [N, K * bits / 32] (uint32 bit patterns), scales are
+ *     fp16 [N, K / group_size], zeros are fp16 [N, K / group_size] when
+ *     asymmetric and NULL when symmetric; codes are unsigned and symmetric
+ *     codes are biased by 2^(bits-1); `interleaved` selects the reference's
+ *     _INTERLEAVE slot order (dequant/packer.py:37-41).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *     asynchronous on that stream, allocates nothing, never synchronises and
+ *     never reads device data on the host, so it can be captured in a CUDA
+ *     graph.
+ *   - Return value: DQG_OK (0) or a non-zero dqg_status; the message of the
+ *     most recent failure on the calling thread is dqg_last_error(). Invalid
+ *     arguments are rejected before anything is launched.
+ */
+#ifndef DEQUANT_B200_H_
+#define DEQUANT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dqg_status {
+  DQG_OK = 0,
+  DQG_ERR_INVALID = 1,     /* argument rejected (shape, format, alignment, pointer) */
+  DQG_ERR_UNSUPPORTED = 2, /* valid but outside what this build handles */
+  DQG_ERR_CUDA = 3         /* a CUDA runtime call failed */
+} dqg_status;
+
+/* Human-readable message of the last failure on this thread ("" if none). */
+const char *dqg_last_error(void);
+
+/* ABI version of this header/library pair (major * 100 + minor). */
+int dqg_version(void);
+
+/*
+ * out[i] = x[i] + 1 for n fp32 values.
+ * Replaces add_one (kernels/smoke.cu:15-25, bound at kernels/bindings.cpp:6),
+ * the reference's toolchain smoke test.
+ */
+int dqg_add_one(const float *x, float *out, int64_t n, void *stream);
+
+/*
+ * y = x @ W^T for a packed W: x fp16 [M, K] row-major with 1 <= M <= 8,
+ * y fp16 [M, N] row-major, fp32 accumulation.
+ * Replaces gemv (kernels/dequant_cuda.h:12-15, kernels/dequant_gemv.cu:339-386,
+ * bound at kernels/bindings.cpp:8-11) with the same checks:
+ *   bits in {2, 4, 8}; group_size > 0; K % group_size == 0;
+ *   group_size % (128 / bits) == 0 (so INT2 with group 32 is rejected);
+ *   zeros != NULL exactly when symmetric == 0; x 16-byte aligned.
+ * Additionally qweight must be 16-byte aligned (it is streamed with bulk
+ * copies). group_size == K is per-channel quantisation.
+ */
+int dqg_gemv(const void *x, const int32_t *qweight, const void *scales, const void *zeros,
+             void *y, int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+             int symmetric, int interleaved, void *stream);
+
+/*
+ * out = dequantize(W) as fp16 [N, K], bit-exact with packer.dequantize.
+ * Replaces dequantize (kernels/dequant_cuda.h:17-20,
+ * kernels/dequant_gemv.cu:310-337, bound at kernels/bindings.cpp:13-16):
+ *   bits in {2, 4, 8}; group_size > 0; K % group_size == 0;
+ *   group_size % (32 / bits) == 0; zeros != NULL exactly when symmetric == 0.
+ */
+int dqg_dequantize(const int32_t *qweight, const void *scales, const void *zeros, void *out,
+                   int64_t N, int64_t K, int64_t bits, int64_t group_size, int symmetric,
+                   int interleaved, void *stream);
+
+/*
+ * Device-side status word of `device` (bit 0: a kernel gave up a bounded
+ * wait). Synchronous; for tests and diagnostics, not for the hot path.
+ * If reset != 0 the word is cleared after reading. No reference counterpart:
+ * the reference kernels have no waits.
+ */
+int dqg_device_status(int device, uint32_t *status, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DEQUANT_B200_H_ */
