@@ -61,14 +61,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
       : "memory");
 }
 
+// Suspend-time hint for try_wait (ns): a waiting warp sleeps in hardware
+// until the phase completes (or this much time passes) instead of spinning
+// and taking issue slots from the warps that do the work.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -106,6 +111,29 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// 2D tiled TMA load of box {x, y} (x = innermost coordinate in elements) from
+// the tensor described by `tmap` (a __grid_constant__ CUtensorMap) into this
+// CTA's shared memory, completing as transaction bytes on `bar`. No
+// multicast. x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Programmatic dependent launch: let the next grid in the stream start its
+// prologue (it still waits for this grid before reading our outputs), and wait
+// for the previous grid before reading anything it may have produced.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // L2 policies for the bulk copies: packed weights are streamed exactly once

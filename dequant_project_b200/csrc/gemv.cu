@@ -146,17 +146,26 @@ struct Vec<16> {
   }
 };
 
-struct RowBlock {
-  int r0, R;
-};
+}  // namespace
 
-__device__ __forceinline__ RowBlock row_block(int r_begin, int rows, int n_rb, int b) {
-  const int a = r_begin + static_cast<int>(static_cast<int64_t>(rows) * b / n_rb);
-  const int e = r_begin + static_cast<int>(static_cast<int64_t>(rows) * (b + 1) / n_rb);
-  return {a, e - a};
+// Physical row (within a 16-row tile) held by MMA row slot g (and g + 8). The
+// packed rows arrive through a 128-byte-swizzled TMA box, where 16-byte unit u
+// of row r sits at unit u ^ (r & 7); this slot order makes the rows that one
+// shared-memory wavefront serves land on disjoint units for each load width.
+template <int WPL>
+__device__ __forceinline__ int slot_row(int g) {
+  if constexpr (WPL == 4) return (g >> 1) | ((g & 1) << 2);   // 0 4 1 5 2 6 3 7
+  else if constexpr (WPL == 2) return ((g & 3) << 1) | (g >> 2);  // 0 2 4 6 1 3 5 7
+  else return g;
 }
 
-}  // namespace
+// Byte offset of packed byte `wb` of tile row `rl` (0..15) in the stage's W
+// area, laid out as boxes [chunk q][tile h][16 rows x 128 B], swizzled.
+__device__ __forceinline__ int w_offset(int h, int rl, int wb) {
+  const int q = wb >> 7;
+  const int u = (wb >> 4) & 7;
+  return ((q * 2 + h) << 11) + (rl << 7) + ((u ^ (rl & 7)) << 4) + (wb & 15);
+}
 
 template <int BITS, bool SYM, bool INTER, int WPL>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
@@ -170,20 +179,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   constexpr int STEP_XB = 4 * LXB;
   constexpr int BIAS = 1 << (BITS - 1);
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled TMA boxes need 1024-byte aligned destinations.
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* full_w = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* full_aux = full_w + kMaxStages;
   uint64_t* empty = full_aux + kMaxStages;
   uint64_t* red_bar = empty + kMaxStages;
+  uint64_t* meta_full = red_bar + 2;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.stages;
 
-  const int r_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
-  const int r_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
-  const int rows = r_end - r_begin;
-  const int n_rb = (rows + kRowBlock - 1) / kRowBlock;
+  // This CTA's tiles (16 rows each, aligned), grouped in row blocks of two.
+  const int T = (p.N + kTile - 1) / kTile;
+  const int t_begin = static_cast<int>(static_cast<int64_t>(T) * blockIdx.x / gridDim.x);
+  const int t_end = static_cast<int>(static_cast<int64_t>(T) * (blockIdx.x + 1) / gridDim.x);
+  const int n_rb = (t_end - t_begin + 1) / 2;
+  const int total = n_rb * p.n_slabs;
+  auto block_rows = [&](int b, int& r0, int& R, int& ntb) {
+    const int t0 = t_begin + 2 * b;
+    ntb = min(2, t_end - t0);
+    r0 = t0 * kTile;
+    R = min(ntb * kTile, p.N - r0);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -193,175 +213,254 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     }
     mbar_init(&red_bar[0], kNCW * 32);
     mbar_init(&red_bar[1], kNCW * 32);
+    mbar_init(&meta_full[0], 1);
+    mbar_init(&meta_full[1], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
-    const uint8_t* qw = reinterpret_cast<const uint8_t*>(p.qw);
-    const int64_t row_bytes = static_cast<int64_t>(p.K) * BITS / 8;
-    int s = 0;
-    bool ok = true;
-    for (int b = 0; b < n_rb && ok; ++b) {
-      const RowBlock rb = row_block(r_begin, rows, n_rb, b);
-      for (int j = 0; j < p.n_slabs; ++j) {
-        const int slot = s % S;
-        if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) {
-          ok = false;
-          break;
-        }
-        const int k0 = j * p.KS;
-        const int L = min(p.KS, p.K - k0);
-        const uint32_t wbytes = static_cast<uint32_t>(L) * BITS / 8;
-        const uint32_t xbytes = static_cast<uint32_t>(L) * 2;
-        uint8_t* st = smem + slot * p.stage_bytes;
-        if (lane == 0) mbar_arrive_expect_tx(&full_w[slot], rb.R * wbytes + p.M * xbytes);
-        __syncwarp();
-        if (lane < rb.R) {
-          bulk_g2s(st + p.off_w + lane * p.w_pitch,
-                   qw + (rb.r0 + lane) * row_bytes + static_cast<int64_t>(k0) * BITS / 8, wbytes,
-                   &full_w[slot], pol_w);
-        }
-        if (lane < p.M) {
-          bulk_g2s(st + p.off_xraw + lane * p.xraw_pitch,
-                   p.x + static_cast<int64_t>(lane) * p.K + k0, xbytes, &full_w[slot], pol_x);
-        }
-        ++s;
+    const int64_t span_elems = static_cast<int64_t>(p.G);
+    // Scales/zeros of a row block: rows [r0, r0 + R) x all groups are one
+    // contiguous span; r0 is a multiple of 16, so it starts 16-byte aligned.
+    // The 16-byte-aligned prefix comes by bulk copy, the rest (only in the
+    // matrix's last partial tile) is read by the aux warps.
+    auto issue_meta = [&](int b) {
+      int r0, R, ntb;
+      block_rows(b, r0, R, ntb);
+      const uint32_t bytes = static_cast<uint32_t>(R * span_elems * 2) & ~15u;
+      uint8_t* dst = smem + p.off_meta + (b & 1) * p.meta_stride;
+      if (lane == 0)
+        mbar_arrive_expect_tx(&meta_full[b & 1], SYM ? bytes : 2 * bytes);
+      __syncwarp();
+      if (bytes) {
+        if (lane == 0)
+          bulk_g2s(dst, p.scales + static_cast<int64_t>(r0) * span_elems, bytes, &meta_full[b & 1],
+                   pol_x);
+        if (!SYM && lane == 1)
+          bulk_g2s(dst + p.meta_stride / 2, p.zeros + static_cast<int64_t>(r0) * span_elems, bytes,
+                   &meta_full[b & 1], pol_x);
       }
+    };
+    auto issue_w = [&](int s, bool with_x) {
+      const int b = s / p.n_slabs, j = s - (s / p.n_slabs) * p.n_slabs;
+      int r0, R, ntb;
+      block_rows(b, r0, R, ntb);
+      const int k0 = j * p.KS;
+      const int L = min(p.KS, p.K - k0);
+      const int nch = (L * BITS / 8 + 127) >> 7;
+      const int slot = s % S;
+      uint8_t* st = smem + slot * p.stage_bytes;
+      if (p.meta_direct && j == 0) issue_meta(b);
+      if (lane == 0)
+        mbar_arrive_expect_tx(&full_w[slot],
+                              static_cast<uint32_t>(ntb * nch * 2048 + p.M * L * 2));
+      __syncwarp();
+      if (lane < nch * ntb) {
+        const int q = lane / ntb, h = lane - (lane / ntb) * ntb;
+        tma_load_2d(st + p.off_w + ((q * 2 + h) << 11), &p.tmap, k0 / PP + 32 * q,
+                    r0 + kTile * h, &full_w[slot], pol_w);
+      }
+      (void)R;
+      if (with_x && lane < p.M)
+        bulk_g2s(st + p.off_xraw + lane * p.xraw_pitch, p.x + static_cast<int64_t>(lane) * p.K + k0,
+                 static_cast<uint32_t>(L) * 2, &full_w[slot], pol_x);
+    };
+    auto issue_x = [&](int s) {
+      const int j = s % p.n_slabs;
+      const int k0 = j * p.KS;
+      const int L = min(p.KS, p.K - k0);
+      uint8_t* st = smem + (s % S) * p.stage_bytes;
+      if (lane < p.M)
+        bulk_g2s(st + p.off_xraw + lane * p.xraw_pitch, p.x + static_cast<int64_t>(lane) * p.K + k0,
+                 static_cast<uint32_t>(L) * 2, &full_w[s % S], pol_x);
+    };
+    // A stage needs no wait if its slot is fresh and, when it starts a row
+    // block, that block's metadata buffer is fresh too (blocks 0 and 1).
+    int pre = min(S, total);
+    if (p.meta_direct) pre = min(pre, 2 * p.n_slabs);
+    // Packed weights and their metadata do not depend on the previous grid:
+    // stream the first stages before waiting for it; activations only after.
+    for (int s = 0; s < pre; ++s) issue_w(s, false);
+    pdl_wait_prior_grid();
+    for (int s = 0; s < pre; ++s) issue_x(s);
+    int s = pre;
+    for (; s < total; ++s) {
+      const int slot = s % S;
+      if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) break;
+      const int b = s / p.n_slabs;
+      if (p.meta_direct && b >= 2 && s == b * p.n_slabs) {
+        // Metadata buffer (b & 1) is free once block b - 2 is fully consumed,
+        // i.e. its last stage t is released. When t <= s - S the ring wait
+        // above already implied that (stages are released in order); only
+        // otherwise is t's slot still on its phase for stage t.
+        const int t = (b - 1) * p.n_slabs - 1;
+        if (t > s - S && !warp_wait(&empty[t % S], (t / S) & 1)) break;
+      }
+      issue_w(s, true);
     }
     // Drain: every copy issued by this warp has landed before the CTA can exit.
     for (int t = max(0, s - S); t < s; ++t) mbar_wait(&full_w[t % S], (t / S) & 1);
+    if (p.meta_direct) {
+      const int nb_issued = (s + p.n_slabs - 1) / p.n_slabs;
+      for (int bb = max(0, nb_issued - 2); bb < nb_issued; ++bb)
+        mbar_wait(&meta_full[bb & 1], (bb >> 1) & 1);
+    }
   } else if (warp <= kNAux) {
     // ----------------------------------------------------------------- aux
     const int a = warp - 1;
-    int s = 0;
-    for (int b = 0; b < n_rb; ++b) {
-      const RowBlock rb = row_block(r_begin, rows, n_rb, b);
-      for (int j = 0; j < p.n_slabs; ++j, ++s) {
-        if (s % kNAux != a) continue;
-        const int slot = s % S;
-        if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) return;
-        const int k0 = j * p.KS;
-        const int L = min(p.KS, p.K - k0);
-        const int G0 = k0 / p.gsize;
-        const int koff = k0 - G0 * p.gsize;
-        const int gps = (koff + L - 1) / p.gsize + 1;
-        uint8_t* st = smem + slot * p.stage_bytes;
-
-        // Per-(row, group) constants: {K0, K1, K2} half2 and fp32 scale.
-        const int n_ent = rb.R * gps;
-        const uint32_t gps_magic = gps == 1 ? 0u : static_cast<uint32_t>((0x100000000ull + gps - 1) / gps);
-        uint16_t sv[kMaxEntPerLane], zv[kMaxEntPerLane];
+    for (int s = a; s < total; s += kNAux) {
+      const int b = s / p.n_slabs, j = s - (s / p.n_slabs) * p.n_slabs;
+      int r0, R, ntb;
+      block_rows(b, r0, R, ntb);
+      const int slot = s % S;
+      const int k0 = j * p.KS;
+      const int L = min(p.KS, p.K - k0);
+      const int G0 = k0 / p.gsize;
+      const int koff = k0 - G0 * p.gsize;
+      const int gps = (koff + L - 1) / p.gsize + 1;
+      const int n_ent = R * gps;
+      const uint32_t gps_magic =
+          gps == 1 ? 0u : static_cast<uint32_t>((0x100000000ull + gps - 1) / gps);
+      uint16_t sv[kMaxEntPerLane], zv[kMaxEntPerLane];
+      if (p.meta_direct) {
+        // This row block's scales/zeros are in shared memory (bulk copy).
+        if (!warp_wait(&meta_full[b & 1], (b >> 1) & 1)) return;
+        const uint16_t* ms = reinterpret_cast<const uint16_t*>(smem + p.off_meta +
+                                                                (b & 1) * p.meta_stride);
+        const uint16_t* mz = ms + p.meta_stride / 4;
+        const int64_t in_smem = (static_cast<int64_t>(R) * p.G * 2 & ~15ll) / 2;
 #pragma unroll
         for (int i = 0; i < kMaxEntPerLane; ++i) {
           const int e = lane + 32 * i;
           if (e < n_ent) {
             const int r = static_cast<int>(fast_div(e, gps_magic));
             const int gl = e - r * gps;
-            const int64_t idx = static_cast<int64_t>(rb.r0 + r) * p.G + G0 + gl;
+            const int64_t li = static_cast<int64_t>(r) * p.G + G0 + gl;
+            const int64_t idx = static_cast<int64_t>(r0) * p.G + li;
+            sv[i] = li < in_smem ? ms[li] : __ldg(p.scales + idx);
+            if constexpr (!SYM) zv[i] = li < in_smem ? mz[li] : __ldg(p.zeros + idx);
+          }
+        }
+      } else {
+        // Scales and zero-points are weights: fetch them before waiting for
+        // the slot, so that their latency overlaps the wait.
+#pragma unroll
+        for (int i = 0; i < kMaxEntPerLane; ++i) {
+          const int e = lane + 32 * i;
+          if (e < n_ent) {
+            const int r = static_cast<int>(fast_div(e, gps_magic));
+            const int gl = e - r * gps;
+            const int64_t idx = static_cast<int64_t>(r0 + r) * p.G + G0 + gl;
             sv[i] = __ldg(p.scales + idx);
             if constexpr (!SYM) zv[i] = __ldg(p.zeros + idx);
           }
         }
-        bool flag = false;
-#pragma unroll
-        for (int i = 0; i < kMaxEntPerLane; ++i) {
-          const int e = lane + 32 * i;
-          if (e < n_ent) {
-            const int r = static_cast<int>(fast_div(e, gps_magic));
-            const int gl = e - r * gps;
-            float zf, zc;
-            if constexpr (SYM) {
-              zf = zc = static_cast<float>(BIAS);
-            } else {
-              zf = __half2float(__ushort_as_half(zv[i]));
-              zc = fminf(fmaxf(rintf(zf), -1024.f), 1024.f);
-            }
-            const float d = zc - zf;
-            const float scale = __half2float(__ushort_as_half(sv[i]));
-            const uint32_t h0 = __half_as_ushort(__float2half_rn(-(1024.f + zc)));
-            const uint32_t h1 = __half_as_ushort(__float2half_rn(-(256.f + zc)));
-            const uint32_t h2 = __half_as_ushort(__float2half_rn(-(64.f + zc)));
-            uint4 ent;
-            ent.x = h0 | (h0 << 16);
-            ent.y = h1 | (h1 << 16);
-            ent.z = h2 | (h2 << 16);
-            ent.w = __float_as_uint(scale);
-            reinterpret_cast<uint4*>(st + p.off_const)[r * p.gps_max + gl] = ent;
-            reinterpret_cast<float*>(st + p.off_corr)[r * p.gps_max + gl] = scale * d;
-            flag |= (d != 0.f);  // NaN compares unequal, so a NaN zero takes this path too
-          }
-        }
-        flag = __any_sync(0xffffffffu, flag);
-
-        // Activations: wait for the raw slab, rewrite it in unpack order.
-        if (!warp_wait(&full_w[slot], (s / S) & 1)) return;
-        const int words = L / PP;
-        for (int n = 0; n < p.M; ++n) {
-          const uint8_t* xr = st + p.off_xraw + n * p.xraw_pitch;
-          uint8_t* xp = st + p.off_xperm + n * p.xperm_pitch;
-          for (int wi = lane; wi < words; wi += 32) {
-            uint32_t v[NPAIR];  // natural order: v[i] = (x[2i], x[2i+1])
-            Vec<WB>::ld(xr + wi * WB, v);
-            uint32_t o[NPAIR];
-#pragma unroll
-            for (int t = 0; t < NPAIR; ++t) {
-              const int lo = slot_logical(BITS, INTER, t);
-              const int hi = slot_logical(BITS, INTER, t + NPAIR);
-              // low half <- x[lo] from v[lo/2], high half <- x[hi] from v[hi/2]
-              o[t] = prmt(v[lo >> 1], v[hi >> 1],
-                          ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
-            }
-            const int stp = wi / (4 * WPL);
-            const int q = wi - stp * (4 * WPL);
-            const int c = q / WPL;
-            const int jj = q - c * WPL;
-            uint8_t* base = xp + stp * STEP_XB + c * U;
-            if constexpr (WB >= U) {
-#pragma unroll
-              for (int piece = 0; piece < WB / U; ++piece) {
-                const int u = (jj * WB) / U + piece;
-                if constexpr (U == 16) {
-                  *reinterpret_cast<uint4*>(base + u * 4 * U) =
-                      make_uint4(o[piece * 4 + 0], o[piece * 4 + 1], o[piece * 4 + 2],
-                                 o[piece * 4 + 3]);
-                } else {
-                  *reinterpret_cast<uint2*>(base + u * 4 * U) = make_uint2(o[0], o[1]);
-                }
-              }
-            } else {
-              // WB == 8 < U == 16: two words share one 16-byte unit.
-              const int u = (jj * WB) / U;
-              *reinterpret_cast<uint2*>(base + u * 4 * U + (jj * WB) % U) = make_uint2(o[0], o[1]);
-            }
-          }
-        }
-        if (flag) {
-          // Per-step activation sums for the zero-point residual.
-          const int steps = L / SC;
-          for (int e = lane; e < p.M * steps; e += 32) {
-            const int n = e / steps;
-            const int stp = e - n * steps;
-            const __half* xr =
-                reinterpret_cast<const __half*>(st + p.off_xraw + n * p.xraw_pitch) + stp * SC;
-            float sum = 0.f;
-            for (int k = 0; k < SC; ++k) sum += __half2float(xr[k]);
-            reinterpret_cast<float*>(st + p.off_sx)[n * p.steps_max + stp] = sum;
-          }
-        }
-        if (lane == 0) *reinterpret_cast<int*>(st + p.off_flag) = flag ? 1 : 0;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full_aux[slot]);
       }
+      if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) return;
+      uint8_t* st = smem + slot * p.stage_bytes;
+      bool flag = false;
+#pragma unroll
+      for (int i = 0; i < kMaxEntPerLane; ++i) {
+        const int e = lane + 32 * i;
+        if (e < n_ent) {
+          const int r = static_cast<int>(fast_div(e, gps_magic));
+          const int gl = e - r * gps;
+          float zf, zc;
+          if constexpr (SYM) {
+            zf = zc = static_cast<float>(BIAS);
+          } else {
+            zf = __half2float(__ushort_as_half(zv[i]));
+            zc = fminf(fmaxf(rintf(zf), -1024.f), 1024.f);
+          }
+          const float d = zc - zf;
+          const float scale = __half2float(__ushort_as_half(sv[i]));
+          const uint32_t h0 = __half_as_ushort(__float2half_rn(-(1024.f + zc)));
+          const uint32_t h1 = __half_as_ushort(__float2half_rn(-(256.f + zc)));
+          const uint32_t h2 = __half_as_ushort(__float2half_rn(-(64.f + zc)));
+          uint4 ent;
+          ent.x = h0 | (h0 << 16);
+          ent.y = h1 | (h1 << 16);
+          ent.z = h2 | (h2 << 16);
+          ent.w = __float_as_uint(scale);
+          // [group][row] layout: the 8 rows one consumer load reads are
+          // 8 consecutive 16-byte entries (no bank conflicts).
+          reinterpret_cast<uint4*>(st + p.off_const)[gl * kRowBlock + r] = ent;
+          reinterpret_cast<float*>(st + p.off_corr)[gl * kRowBlock + r] = scale * d;
+          flag |= (d != 0.f);  // NaN compares unequal, so a NaN zero takes this path too
+        }
+      }
+      flag = __any_sync(0xffffffffu, flag);
+
+      // Activations: wait for the raw slab, rewrite it in unpack order.
+      if (!warp_wait(&full_w[slot], (s / S) & 1)) return;
+      const int words = L / PP;
+      for (int n = 0; n < p.M; ++n) {
+        const uint8_t* xr = st + p.off_xraw + n * p.xraw_pitch;
+        uint8_t* xp = st + p.off_xperm + n * p.xperm_pitch;
+        for (int wi = lane; wi < words; wi += 32) {
+          uint32_t v[NPAIR];  // natural order: v[i] = (x[2i], x[2i+1])
+          Vec<WB>::ld(xr + wi * WB, v);
+          uint32_t o[NPAIR];
+#pragma unroll
+          for (int t = 0; t < NPAIR; ++t) {
+            const int lo = slot_logical(BITS, INTER, t);
+            const int hi = slot_logical(BITS, INTER, t + NPAIR);
+            // low half <- x[lo] from v[lo/2], high half <- x[hi] from v[hi/2]
+            o[t] = prmt(v[lo >> 1], v[hi >> 1],
+                        ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
+          }
+          const int stp = wi / (4 * WPL);
+          const int q = wi - stp * (4 * WPL);
+          const int c = q / WPL;
+          const int jj = q - c * WPL;
+          uint8_t* base = xp + stp * STEP_XB + c * U;
+          if constexpr (WB >= U) {
+#pragma unroll
+            for (int piece = 0; piece < WB / U; ++piece) {
+              const int u = (jj * WB) / U + piece;
+              if constexpr (U == 16) {
+                *reinterpret_cast<uint4*>(base + u * 4 * U) =
+                    make_uint4(o[piece * 4 + 0], o[piece * 4 + 1], o[piece * 4 + 2],
+                               o[piece * 4 + 3]);
+              } else {
+                *reinterpret_cast<uint2*>(base + u * 4 * U) = make_uint2(o[0], o[1]);
+              }
+            }
+          } else {
+            // WB == 8 < U == 16: two words share one 16-byte unit.
+            const int u = (jj * WB) / U;
+            *reinterpret_cast<uint2*>(base + u * 4 * U + (jj * WB) % U) = make_uint2(o[0], o[1]);
+          }
+        }
+      }
+      if (flag) {
+        // Per-step activation sums for the zero-point residual.
+        const int steps = L / SC;
+        for (int e = lane; e < p.M * steps; e += 32) {
+          const int n = e / steps;
+          const int stp = e - n * steps;
+          const __half* xr =
+              reinterpret_cast<const __half*>(st + p.off_xraw + n * p.xraw_pitch) + stp * SC;
+          float sum = 0.f;
+          for (int k = 0; k < SC; ++k) sum += __half2float(xr[k]);
+          reinterpret_cast<float*>(st + p.off_sx)[n * p.steps_max + stp] = sum;
+        }
+      }
+      if (lane == 0) *reinterpret_cast<int*>(st + p.off_flag) = flag ? 1 : 0;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_aux[slot]);
     }
   } else {
     // ------------------------------------------------------------ consumers
     const int cw = warp - 1 - kNAux;
     const int gid = lane >> 2;
     const int c = lane & 3;
+    const int prow = slot_row<WPL>(gid);  // physical row of slot gid in a tile
     const bool has_x = gid < p.M;
     float acc[2][4];
 #pragma unroll
@@ -371,7 +470,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 
     int s = 0;
     for (int b = 0; b < n_rb; ++b) {
-      const RowBlock rb = row_block(r_begin, rows, n_rb, b);
+      int r0, R, ntb;
+      block_rows(b, r0, R, ntb);
       for (int j = 0; j < p.n_slabs; ++j, ++s) {
         const int slot = s % S;
         const uint32_t par = (s / S) & 1;
@@ -396,28 +496,34 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 #pragma unroll
             for (int i = 0; i < WPL * NPAIR; ++i) bx[i] = 0u;
           }
+          const int wb = (stp * 4 * WPL + c * WPL) * 4;
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt) {
-            const int ra = mt * 16 + gid;
+            const int ra = mt * kTile + prow;      // physical rows of slots gid, gid + 8
             const int rbw = ra + 8;
-            uint32_t wa[WPL], wb[WPL];
-            const int wofs = (stp * 4 * WPL + c * WPL) * 4;
-            Vec<WPL * 4>::ld(st + p.off_w + ra * p.w_pitch + wofs, wa);
-            Vec<WPL * 4>::ld(st + p.off_w + rbw * p.w_pitch + wofs, wb);
-            const uint4 ca = reinterpret_cast<const uint4*>(st + p.off_const)[ra * p.gps_max + gl];
-            const uint4 cb = reinterpret_cast<const uint4*>(st + p.off_const)[rbw * p.gps_max + gl];
+            uint32_t wa[WPL], wbv[WPL];
+            Vec<WPL * 4>::ld(st + p.off_w + w_offset(mt, prow, wb), wa);
+            Vec<WPL * 4>::ld(st + p.off_w + w_offset(mt, prow + 8, wb), wbv);
+            const uint4 ca = reinterpret_cast<const uint4*>(st + p.off_const)[gl * kRowBlock + ra];
+            const uint4 cb = reinterpret_cast<const uint4*>(st + p.off_const)[gl * kRowBlock + rbw];
+            // Two independent accumulator chains (even / odd MMAs) halve the
+            // dependent-MMA latency of a step; summed once at the end.
             float d[4] = {0.f, 0.f, 0.f, 0.f};
+            float e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int jj = 0; jj < WPL; ++jj) {
               uint32_t pa[NPAIR], pb[NPAIR];
               unpack_pairs<BITS>(wa[jj], ca.x, ca.y, ca.z, pa);
-              unpack_pairs<BITS>(wb[jj], cb.x, cb.y, cb.z, pb);
+              unpack_pairs<BITS>(wbv[jj], cb.x, cb.y, cb.z, pb);
 #pragma unroll
               for (int i = 0; i < NPAIR / 2; ++i) {
-                mma_16816(d, pa[2 * i], pb[2 * i], pa[2 * i + 1], pb[2 * i + 1],
+                float* acc_chain = ((jj * (NPAIR / 2) + i) & 1) ? e : d;
+                mma_16816(acc_chain, pa[2 * i], pb[2 * i], pa[2 * i + 1], pb[2 * i + 1],
                           bx[jj * NPAIR + 2 * i], bx[jj * NPAIR + 2 * i + 1]);
               }
             }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d[i] += e[i];
             const float sa = __uint_as_float(ca.w);
             const float sb = __uint_as_float(cb.w);
             acc[mt][0] = fmaf(sa, d[0], acc[mt][0]);
@@ -429,8 +535,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
               const float* sx = reinterpret_cast<const float*>(st + p.off_sx);
               const float xa = (2 * c < p.M) ? sx[(2 * c) * p.steps_max + stp] : 0.f;
               const float xb = (2 * c + 1 < p.M) ? sx[(2 * c + 1) * p.steps_max + stp] : 0.f;
-              const float qa = corr[ra * p.gps_max + gl];
-              const float qb = corr[rbw * p.gps_max + gl];
+              const float qa = corr[gl * kRowBlock + ra];
+              const float qb = corr[gl * kRowBlock + rbw];
               acc[mt][0] = fmaf(qa, xa, acc[mt][0]);
               acc[mt][1] = fmaf(qa, xb, acc[mt][1]);
               acc[mt][2] = fmaf(qb, xa, acc[mt][2]);
@@ -447,7 +553,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
       float* red = reinterpret_cast<float*>(smem + p.off_red) + buf * (kNCW * kRowBlock * kMaxM);
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        float* rw = red + (cw * kRowBlock + mt * 16 + gid) * kMaxM + 2 * c;
+        float* rw = red + (cw * kRowBlock + mt * kTile + prow) * kMaxM + 2 * c;
         *reinterpret_cast<float2*>(rw) = make_float2(acc[mt][0], acc[mt][1]);
         *reinterpret_cast<float2*>(rw + 8 * kMaxM) = make_float2(acc[mt][2], acc[mt][3]);
 #pragma unroll
@@ -459,12 +565,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
       for (int idx = tc; idx < kRowBlock * p.M; idx += kNCW * 32) {
         const int row = idx & (kRowBlock - 1);
         const int col = idx / kRowBlock;
-        if (row < rb.R) {
+        if (row < R) {
           float sum = 0.f;
 #pragma unroll
           for (int w = 0; w < kNCW; ++w) sum += red[(w * kRowBlock + row) * kMaxM + col];
-          p.y[static_cast<int64_t>(col) * p.N + rb.r0 + row] =
-              __half_as_ushort(__float2half_rn(sum));
+          p.y[static_cast<int64_t>(col) * p.N + r0 + row] = __half_as_ushort(__float2half_rn(sum));
         }
       }
     }
@@ -477,9 +582,23 @@ namespace {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-struct Variant {
-  int wpl;
-};
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
 
 template <int BITS, bool SYM, bool INTER, int WPL>
 cudaError_t launch_variant(const GemvParams& p, int grid, int smem, cudaStream_t stream) {
@@ -488,13 +607,24 @@ cudaError_t launch_variant(const GemvParams& p, int grid, int smem, cudaStream_t
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 64 && configured[dev] < smem) {
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemBytes);
     if (e != cudaSuccess) return e;
-    configured[dev] = kMaxSmemBytes;
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
-  kern<<<grid, kGemvThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  // Programmatic dependent launch: this grid may start while the previous
+  // one drains; the kernel waits for it before touching activations.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int BITS, bool SYM, bool INTER>
@@ -534,35 +664,43 @@ int gemv_words_per_lane(int bits, int group_size, int K) {
 bool plan_gemv(int M, int N, int K, int bits, int group_size, int num_sms, GemvPlan* plan) {
   const int pp = 32 / bits;
   const int wpl = gemv_words_per_lane(bits, group_size, K);
-  if (wpl == 0) return false;
+  if (wpl == 0 || num_sms <= 0) return false;
   const int sc = 4 * wpl * pp;
   const int lxb = wpl * pp * 2;
   const int u = lxb >= 16 ? 16 : lxb;
-  const int budget = kMaxSmemBytes - kRedBytes - kBarBytes;
+  const int chunk_codes = 1024 / bits;  // codes in one 128-byte TMA box row
+  const int budget = kMaxSmemBytes - kRedBytes - kBarBytes - kAlignSlack;
   // Slab length depends only on the format and K, never on M: the order in
   // which a row's products are summed is then the same for every batch size,
   // so each output row is bit-identical to the M = 1 call on that activation
-  // row. Target 512 packed bytes per row per stage.
-  int ks = (512 * 8 / bits) / sc * sc;
-  if (ks < sc) ks = sc;
+  // row. Target 512 packed bytes per row per stage, in whole 128-byte boxes.
+  int ks = 4096 / bits;
+  while (ks > chunk_codes && (ks + group_size - 1) / group_size + 1 > kMaxEntPerLane)
+    ks -= chunk_codes;
   if (ks > K) ks = K;
-  // Keep the per-stage constant table within the aux warps' register budget.
-  while (ks > sc && (ks + group_size - 1) / group_size + 1 > kMaxEntPerLane) ks -= sc;
+  if (ks % sc != 0) return false;
   const int G = K / group_size;
   int gps_max = (ks % group_size == 0) ? ks / group_size : (ks + group_size - 1) / group_size + 1;
   if (gps_max > G) gps_max = G;
   if (gps_max < 1) gps_max = 1;
+  if (gps_max > kMaxEntPerLane) return false;
   GemvPlan pl;
   pl.wpl = wpl;
   pl.ks = ks;
   pl.gps_max = gps_max;
   pl.steps_max = ks / sc;
-  pl.w_pitch = round_up(ks * bits / 8, 128) + 16 * wpl;
   pl.xraw_pitch = ks * 2;
   pl.xperm_pitch = round_up(ks * 2, 128) + (u == 16 ? 64 : 32);
+  const int nch = (ks * bits / 8 + 127) / 128;
+  // Two row-block metadata buffers, each [scales span | zeros span] of
+  // 32 rows x G fp16 (the span is copied whole when it fits the budget).
+  const int span = round_up(kRowBlock * G * 2, 128);
+  const int meta_stride = 2 * span;
+  const bool meta_direct = 2 * meta_stride <= kMaxMetaBytes;
+  const int meta_bytes = meta_direct ? 2 * meta_stride : 0;
   int off = 0;
   pl.off_w = off;
-  off += kRowBlock * pl.w_pitch;
+  off += 2 * nch * 2048;
   pl.off_xraw = off;
   off += round_up(M * pl.xraw_pitch, 128);
   pl.off_xperm = off;
@@ -575,21 +713,37 @@ bool plan_gemv(int M, int N, int K, int bits, int group_size, int num_sms, GemvP
   off += round_up(M * pl.steps_max * 4, 128);
   pl.off_flag = off;
   off += 128;
+  off = round_up(off, 1024);
   pl.stage_bytes = off;
-  int stages = budget / off;
+  int stages = (budget - meta_bytes) / off;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
   pl.stages = stages;
-  pl.off_red = stages * off;
+  pl.meta_direct = meta_direct ? 1 : 0;
+  pl.off_meta = stages * off;
+  pl.meta_stride = meta_stride;
+  pl.off_red = pl.off_meta + meta_bytes;
   pl.off_bar = pl.off_red + kRedBytes;
-  pl.smem = pl.off_bar + kBarBytes;
-  pl.grid = N < num_sms ? N : num_sms;
+  pl.smem = pl.off_bar + kBarBytes + kAlignSlack;
+  const int tiles = (N + kTile - 1) / kTile;
+  pl.grid = tiles < num_sms ? tiles : num_sms;
   *plan = pl;
   return true;
 }
 
 cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& pl, cudaStream_t stream) {
   GemvParams p;
+  EncodeTiledFn enc = encode_tiled();
+  if (enc == nullptr) return cudaErrorNotSupported;
+  const cuuint64_t words = static_cast<cuuint64_t>(a.K) * a.bits / 32;
+  const cuuint64_t dims[2] = {words, static_cast<cuuint64_t>(a.N)};
+  const cuuint64_t strides[1] = {words * 4};
+  const cuuint32_t box[2] = {32, kTile};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<uint32_t*>(a.qweight), dims,
+          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
   p.x = a.x;
   p.qw = a.qweight;
   p.scales = a.scales;
@@ -608,7 +762,6 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& pl, cudaStream_t stre
   p.gq_magic = gq <= 1 ? 0u : static_cast<uint32_t>((0x100000000ull + gq - 1) / gq);
   p.gps_max = pl.gps_max;
   p.steps_max = pl.steps_max;
-  p.w_pitch = pl.w_pitch;
   p.xraw_pitch = pl.xraw_pitch;
   p.xperm_pitch = pl.xperm_pitch;
   p.off_w = pl.off_w;
@@ -621,6 +774,12 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& pl, cudaStream_t stre
   p.stage_bytes = pl.stage_bytes;
   p.off_red = pl.off_red;
   p.off_bar = pl.off_bar;
+  // Metadata bulk copies need 16-byte-aligned tensors; otherwise the aux
+  // warps read scales/zeros from global memory.
+  p.meta_direct = pl.meta_direct && reinterpret_cast<uintptr_t>(a.scales) % 16 == 0 &&
+                  (a.zeros == nullptr || reinterpret_cast<uintptr_t>(a.zeros) % 16 == 0);
+  p.off_meta = pl.off_meta;
+  p.meta_stride = pl.meta_stride;
 
 #define DQG_GEMV_CASE(B, S, I) \
   if (a.bits == B && a.symmetric == S && a.interleaved == I) \

@@ -4,11 +4,13 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>  // CUtensorMap (the encoder is fetched through the runtime)
 #include <cuda_runtime.h>
 
 namespace dqg {
 
-constexpr int kRowBlock = 32;     // output rows per row block (two m16 tiles)
+constexpr int kTile = 16;         // rows per tile (one m16 MMA tile, one TMA box)
+constexpr int kRowBlock = 32;     // output rows per row block (two tiles)
 constexpr int kNCW = 8;           // consumer (tensor-core) warps
 constexpr int kNAux = 4;          // constant/activation-permute warps
 constexpr int kGemvThreads = 32 * (1 + kNAux + kNCW);
@@ -18,8 +20,11 @@ constexpr int kMaxEntPerLane = 17;  // (row, group) constants per aux lane per s
 constexpr int kMaxSmemBytes = 232448;  // 227 KB opt-in dynamic shared memory
 constexpr int kRedBytes = 2 * kNCW * kRowBlock * kMaxM * 4;
 constexpr int kBarBytes = 256;
+constexpr int kAlignSlack = 1024;
+constexpr int kMaxMetaBytes = 96 * 1024;  // cap on the two row-block metadata buffers   // dynamic smem is re-aligned to 1024 bytes
 
 struct GemvParams {
+  CUtensorMap tmap;         // packed words [N rows, K*bits/32 words], 32x16 boxes, 128B swizzle
   const uint16_t* x;        // fp16 [M, K]
   const uint32_t* qw;       // packed words [N, K*bits/32]
   const uint16_t* scales;   // fp16 [N, G]
@@ -32,10 +37,12 @@ struct GemvParams {
   uint32_t gq_magic;        // fast_div magic for group_size / step codes
   int gps_max;              // constant entries per row per stage
   int steps_max;            // steps per slab
-  int w_pitch, xraw_pitch, xperm_pitch;
+  int xraw_pitch, xperm_pitch;
   int off_w, off_xraw, off_xperm, off_const, off_corr, off_sx, off_flag;
   int stage_bytes;
   int off_red, off_bar;
+  int meta_direct;          // 1: row-block metadata arrives by bulk copy into off_meta
+  int off_meta, meta_stride;  // two buffers, each [scales span | zeros span]
 };
 
 struct GemvArgs {
@@ -50,9 +57,10 @@ struct GemvArgs {
 
 struct GemvPlan {
   int wpl, ks, gps_max, steps_max, stages;
-  int w_pitch, xraw_pitch, xperm_pitch;
+  int xraw_pitch, xperm_pitch;
   int off_w, off_xraw, off_xperm, off_const, off_corr, off_sx, off_flag;
   int stage_bytes, off_red, off_bar, smem, grid;
+  int meta_direct, off_meta, meta_stride;
 };
 
 // Words of packed codes each lane loads per step (4, 2 or 1), or 0 when the

@@ -184,6 +184,30 @@ def test_zero_point_edge_cases(bits, zkind):
         check_against_oracle(x[:m], qw, s, z, bits, gs, False, "sequential", y)
 
 
+@pytest.mark.parametrize("bits,gs", [(4, 128), (2, 64), (8, None)])
+def test_unaligned_metadata_takes_the_plain_load_path(bits, gs):
+    """Scales/zeros that are only 2-byte aligned cannot be bulk-copied; the
+    kernel reads them from global memory instead, with identical results."""
+    torch.manual_seed(11)
+    n, k = 1000, 2048
+    w = (torch.randn(n, k, dtype=torch.float16) * 0.02).numpy()
+    x = torch.randn(4, k, dtype=torch.float16).numpy()
+    qw, s, z = pack_np(w, bits, gs, False, "sequential")
+    xd, qd, sd, zd = to_dev(x, qw, s, z)
+    y_aligned = dequant_cuda.gemv(xd, qd, sd, zd, bits, gs or k, False, False)
+    # Same values at an address that is 2 mod 16.
+    s_buf = torch.empty(sd.numel() + 1, dtype=torch.float16, device="cuda")
+    z_buf = torch.empty(zd.numel() + 1, dtype=torch.float16, device="cuda")
+    s_off = s_buf[1:].view(sd.shape)
+    z_off = z_buf[1:].view(zd.shape)
+    s_off.copy_(sd)
+    z_off.copy_(zd)
+    assert s_off.data_ptr() % 16 == 2
+    y_off = dequant_cuda.gemv(xd, qd, s_off, z_off, bits, gs or k, False, False)
+    assert torch.equal(y_aligned, y_off)
+    check_against_oracle(x, qw, s, z, bits, gs, False, "sequential", y_off.cpu().numpy())
+
+
 def test_rejections():
     """INT2 g32 and M=9 raise RuntimeError (scripts/test_dequant_kernel.py:174-191)."""
     dev = "cuda"
