@@ -163,11 +163,6 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   rc = check_device_ptr(y, dev, "y");
   if (rc) return rc;
 
-  dqg::GemvPlan plan;
-  if (!dqg::plan_gemv(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-                      static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev), &plan))
-    return fail(DQG_ERR_UNSUPPORTED, "no shared-memory plan for M=%lld K=%lld bits=%lld group=%lld",
-                (long long)M, (long long)K, (long long)bits, (long long)group_size);
   dqg::GemvArgs a;
   a.x = static_cast<const uint16_t*>(x);
   a.qweight = reinterpret_cast<const uint32_t*>(qweight);
@@ -181,6 +176,24 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   a.group_size = static_cast<int>(group_size);
   a.symmetric = symmetric != 0;
   a.interleaved = interleaved != 0;
+  // The streaming kernel whenever its plan fits (activations resident in
+  // shared memory, 16-byte-aligned scales/zeros); the general kernel otherwise.
+  dqg::StreamPlan splan;
+  const bool meta_aligned = reinterpret_cast<uintptr_t>(scales) % 16 == 0 &&
+                            (zeros == nullptr || reinterpret_cast<uintptr_t>(zeros) % 16 == 0);
+  if (meta_aligned &&
+      dqg::plan_stream(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                       static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
+                       &splan)) {
+    e = dqg::launch_stream(a, splan, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    return ok();
+  }
+  dqg::GemvPlan plan;
+  if (!dqg::plan_gemv(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                      static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev), &plan))
+    return fail(DQG_ERR_UNSUPPORTED, "no shared-memory plan for M=%lld K=%lld bits=%lld group=%lld",
+                (long long)M, (long long)K, (long long)bits, (long long)group_size);
   e = dqg::launch_gemv(a, plan, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
   return ok();

@@ -113,19 +113,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-// 2D tiled TMA load of box {x, y} (x = innermost coordinate in elements) from
-// the tensor described by `tmap` (a __grid_constant__ CUtensorMap) into this
-// CTA's shared memory, completing as transaction bytes on `bar`. No
-// multicast. x * element size must be a multiple of 16 bytes.
-__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y,
-                                            uint64_t* bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
 // Programmatic dependent launch: let the next grid in the stream start its
 // prologue (it still waits for this grid before reading our outputs), and wait
 // for the previous grid before reading anything it may have produced.
@@ -178,6 +165,22 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
+}
+
+// Interleaved slot orders (dequant/packer.py:37-41): slot s of a word holds
+// logical code order[s] of that word.
+__host__ __device__ constexpr int slot_logical(int bits, bool inter, int s) {
+  if (!inter) return s;
+  if (bits == 4) {
+    constexpr int o[8] = {0, 2, 4, 6, 1, 3, 5, 7};
+    return o[s];
+  }
+  if (bits == 2) {
+    constexpr int o[16] = {0, 4, 8, 12, 1, 5, 9, 13, 2, 6, 10, 14, 3, 7, 11, 15};
+    return o[s];
+  }
+  constexpr int o[4] = {0, 2, 1, 3};
+  return o[s];
 }
 
 // floor(n / d) for n < 2^16 and 1 <= d < 2^16, with magic = ceil(2^32 / d)

@@ -4,27 +4,25 @@
 #pragma once
 
 #include <cstdint>
-#include <cuda.h>  // CUtensorMap (the encoder is fetched through the runtime)
 #include <cuda_runtime.h>
 
 namespace dqg {
 
-constexpr int kTile = 16;         // rows per tile (one m16 MMA tile, one TMA box)
-constexpr int kRowBlock = 32;     // output rows per row block (two tiles)
+constexpr int kTile = 16;         // rows per tile (one m16 MMA tile)
 constexpr int kNCW = 8;           // consumer (tensor-core) warps
 constexpr int kNAux = 4;          // constant/activation-permute warps
 constexpr int kGemvThreads = 32 * (1 + kNAux + kNCW);
 constexpr int kMaxStages = 8;
 constexpr int kMaxM = 8;          // activation rows handled by the GEMV path
-constexpr int kMaxEntPerLane = 17;  // (row, group) constants per aux lane per stage
 constexpr int kMaxSmemBytes = 232448;  // 227 KB opt-in dynamic shared memory
-constexpr int kRedBytes = 2 * kNCW * kRowBlock * kMaxM * 4;
+constexpr int kRedBytes = 2 * kNCW * kTile * kMaxM * 4;
+constexpr int kStageBytes = 40 * 1024;     // target packed bytes per 16-row stage
+constexpr int kMaxXresBytes = 100 * 1024;  // cap on resident permuted activations
+constexpr int kXStageBytes = 48 * 1024;    // cap on per-stage raw + permuted activations
 constexpr int kBarBytes = 256;
-constexpr int kAlignSlack = 1024;
-constexpr int kMaxMetaBytes = 96 * 1024;  // cap on the two row-block metadata buffers   // dynamic smem is re-aligned to 1024 bytes
+constexpr int kMaxMetaBytes = 64 * 1024;  // cap on the two tile metadata buffers
 
 struct GemvParams {
-  CUtensorMap tmap;         // packed words [N rows, K*bits/32 words], 32x16 boxes, 128B swizzle
   const uint16_t* x;        // fp16 [M, K]
   const uint32_t* qw;       // packed words [N, K*bits/32]
   const uint16_t* scales;   // fp16 [N, G]
@@ -35,14 +33,16 @@ struct GemvParams {
   int n_slabs;
   int stages;
   uint32_t gq_magic;        // fast_div magic for group_size / step codes
-  int gps_max;              // constant entries per row per stage
+  int ep;                   // constant entries per row (odd stride)
   int steps_max;            // steps per slab
-  int xraw_pitch, xperm_pitch;
-  int off_w, off_xraw, off_xperm, off_const, off_corr, off_sx, off_flag;
+  int w_pitch;              // padded bytes per packed row in a stage
+  int xp_pitch;             // bytes per permuted activation row
+  int off_w, off_xraw, off_xperm, off_ent, off_sx, off_flag;
   int stage_bytes;
+  int off_xres;             // whole-K permuted activations (resident variant)
+  int off_sxres;            // their per-step sums [M][K / step]
+  int off_meta, meta_stride, meta_direct;
   int off_red, off_bar;
-  int meta_direct;          // 1: row-block metadata arrives by bulk copy into off_meta
-  int off_meta, meta_stride;  // two buffers, each [scales span | zeros span]
 };
 
 struct GemvArgs {
@@ -56,11 +56,10 @@ struct GemvArgs {
 };
 
 struct GemvPlan {
-  int wpl, ks, gps_max, steps_max, stages;
-  int xraw_pitch, xperm_pitch;
-  int off_w, off_xraw, off_xperm, off_const, off_corr, off_sx, off_flag;
-  int stage_bytes, off_red, off_bar, smem, grid;
-  int meta_direct, off_meta, meta_stride;
+  int wpl, ks, n_slabs, ep, steps_max, xres, stages;
+  int w_pitch, xp_pitch;
+  int off_w, off_xraw, off_xperm, off_ent, off_sx, off_flag, stage_bytes;
+  int off_xres, off_sxres, off_meta, meta_stride, meta_direct, off_red, off_bar, smem, grid;
 };
 
 // Words of packed codes each lane loads per step (4, 2 or 1), or 0 when the
@@ -71,6 +70,43 @@ int gemv_words_per_lane(int bits, int group_size, int K);
 bool plan_gemv(int M, int N, int K, int bits, int group_size, int num_sms, GemvPlan* plan);
 
 cudaError_t launch_gemv(const GemvArgs& args, const GemvPlan& plan, cudaStream_t stream);
+
+// ---------------------------------------------------------------- streaming
+// Streaming kernel (gemv_stream.cu): activations resident in shared memory,
+// codes unpacked to fp16 subnormals, no preparation warps. Used whenever its
+// plan fits; gemv_kernel above covers the rest (activations too large to keep
+// resident, or very many groups per row).
+constexpr int kStreamNCW = 8;     // consumer (tensor-core) warps
+constexpr int kStreamThreads = 32 * (2 + kStreamNCW);  // + producer + reducer
+constexpr int kStreamNRB = 4;     // tile reduction buffers
+constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations
+constexpr int kStreamStageBytes = 40 * 1024;   // target packed bytes per stage
+constexpr int kStreamMaxFixedBytes = 128 * 1024;  // cap on everything but the ring
+
+struct StreamParams {
+  const uint16_t* x;
+  const uint32_t* qw;
+  const uint16_t* scales;
+  const uint16_t* zeros;
+  uint16_t* y;
+  int M, N, K, G, gsize;
+  int mp;                 // columns per group slot of the MMA's N=8 side (1,2,4,8)
+  int KS, n_slabs, stages;
+  int w_pitch, xp;        // bytes per packed row in a stage; per activation row
+  int stage_bytes;
+  int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar;
+  long long tail_first;   // first scales/zeros element past the last 16-byte boundary
+  int tail_n;             // number of such elements (0..7)
+};
+
+struct StreamPlan {
+  int wpl, mp, ks, n_slabs, stages, w_pitch, xp, stage_bytes;
+  int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar;
+  int smem, grid;
+};
+
+bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, StreamPlan* plan);
+cudaError_t launch_stream(const GemvArgs& args, const StreamPlan& plan, cudaStream_t stream);
 
 struct DequantArgs {
   const uint32_t* qweight;

@@ -187,7 +187,8 @@ def test_zero_point_edge_cases(bits, zkind):
 @pytest.mark.parametrize("bits,gs", [(4, 128), (2, 64), (8, None)])
 def test_unaligned_metadata_takes_the_plain_load_path(bits, gs):
     """Scales/zeros that are only 2-byte aligned cannot be bulk-copied; the
-    kernel reads them from global memory instead, with identical results."""
+    general kernel then reads them from global memory. Both paths meet both
+    criteria."""
     torch.manual_seed(11)
     n, k = 1000, 2048
     w = (torch.randn(n, k, dtype=torch.float16) * 0.02).numpy()
@@ -204,7 +205,7 @@ def test_unaligned_metadata_takes_the_plain_load_path(bits, gs):
     z_off.copy_(zd)
     assert s_off.data_ptr() % 16 == 2
     y_off = dequant_cuda.gemv(xd, qd, s_off, z_off, bits, gs or k, False, False)
-    assert torch.equal(y_aligned, y_off)
+    check_against_oracle(x, qw, s, z, bits, gs, False, "sequential", y_aligned.cpu().numpy())
     check_against_oracle(x, qw, s, z, bits, gs, False, "sequential", y_off.cpu().numpy())
 
 
@@ -248,9 +249,10 @@ def test_negative_control_single_flipped_bit():
 
 
 def test_batch_rows_are_independent_and_deterministic():
-    """Size-independent properties at a full benchmark shape: each output row
-    equals the M=1 call on that activation row bit for bit, and repeated calls
-    are bit-identical."""
+    """Size-independent properties at a full benchmark shape: repeated calls
+    are bit-identical; an output row does not depend on the other activation
+    rows of the batch (bit for bit, same M); and it matches the M=1 call on
+    that activation row to within fp32 summation order."""
     torch.manual_seed(5)
     w = torch.randn(11008, 4096, dtype=torch.float16, device="cuda") * 0.02
     for bits, gs, sym in BENCH:
@@ -259,8 +261,14 @@ def test_batch_rows_are_independent_and_deterministic():
         args = (pw.qweight, pw.scales, pw.zeros, bits, gs or 4096, sym, False)
         y8 = dequant_cuda.gemv(x, *args)
         assert torch.equal(y8, dequant_cuda.gemv(x, *args))
+        x_other = torch.randn(8, 4096, dtype=torch.float16, device="cuda")
         for m in range(8):
-            assert torch.equal(dequant_cuda.gemv(x[m:m + 1].contiguous(), *args)[0], y8[m])
+            mixed = x_other.clone()
+            mixed[m] = x[m]
+            assert torch.equal(dequant_cuda.gemv(mixed, *args)[m], y8[m])
+            y1 = dequant_cuda.gemv(x[m:m + 1].contiguous(), *args)[0].float()
+            d = (y1 - y8[m].float()).abs().max().item()
+            assert d <= 1e-3 * y8[m].float().abs().max().item()
 
 
 def test_graph_capture_replays_live_input():
