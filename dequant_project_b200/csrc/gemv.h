@@ -82,6 +82,8 @@ constexpr int kStreamNRB = 4;     // tile reduction buffers
 constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations
 constexpr int kStreamStageBytes = 40 * 1024;   // target packed bytes per stage
 constexpr int kStreamMaxFixedBytes = 128 * 1024;  // cap on everything but the ring
+constexpr int kStreamMaxMeta = 8;  // tile metadata buffers
+constexpr int kStreamBarBytes = 512;
 
 struct StreamParams {
   const uint16_t* x;
@@ -91,7 +93,7 @@ struct StreamParams {
   uint16_t* y;
   int M, N, K, G, gsize;
   int mp;                 // columns per group slot of the MMA's N=8 side (1,2,4,8)
-  int KS, n_slabs, stages;
+  int KS, n_slabs, stages, n_meta;
   int w_pitch, xp;        // bytes per packed row in a stage; per activation row
   int stage_bytes;
   int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar;
@@ -100,7 +102,7 @@ struct StreamParams {
 };
 
 struct StreamPlan {
-  int wpl, mp, ks, n_slabs, stages, w_pitch, xp, stage_bytes;
+  int wpl, mp, ks, n_slabs, stages, n_meta, w_pitch, xp, stage_bytes;
   int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar;
   int smem, grid;
 };

@@ -212,8 +212,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* meta_full = empty + kMaxStages;     // [2]
-  uint64_t* red_full = meta_full + 2;           // [kStreamNRB]
+  uint64_t* meta_full = empty + kMaxStages;     // [kStreamMaxMeta]
+  uint64_t* red_full = meta_full + kStreamMaxMeta;  // [kStreamNRB]
   uint64_t* red_empty = red_full + kStreamNRB;  // [kStreamNRB]
   uint64_t* x_full = red_empty + kStreamNRB;
   uint64_t* pro_bar = x_full + 1;               // [2] consumer prologue barriers
@@ -221,6 +221,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.stages;
+  const int NMB = p.n_meta;
   const int64_t row_bytes = static_cast<int64_t>(p.K) * BITS / 8;
   const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
   const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
@@ -232,8 +233,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kStreamNCW);
     }
-    mbar_init(&meta_full[0], 1);
-    mbar_init(&meta_full[1], 1);
+    for (int b = 0; b < NMB; ++b) mbar_init(&meta_full[b], 1);
     for (int b = 0; b < kStreamNRB; ++b) {
       mbar_init(&red_full[b], kStreamNCW);
       mbar_init(&red_empty[b], 1);
@@ -269,7 +269,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const int64_t a0 = (e0 * 2) & ~15ll;
       const int64_t a1 = min((e1 * 2 + 15) & ~15ll, p.tail_first * 2);
       const uint32_t bytes = a1 > a0 ? static_cast<uint32_t>(a1 - a0) : 0u;
-      uint8_t* dst = smem + p.off_meta + (i & 1) * p.meta_stride;
+      const int mb = i % NMB;
+      uint8_t* dst = smem + p.off_meta + mb * p.meta_stride;
       if (e1 > p.tail_first) {
         const int64_t e = p.tail_first + lane;
         if (lane < p.tail_n && e >= e0 && e < e1) {
@@ -278,15 +279,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(&meta_full[i & 1], SYM ? bytes : 2 * bytes);
+      if (lane == 0) mbar_arrive_expect_tx(&meta_full[mb], SYM ? bytes : 2 * bytes);
       __syncwarp();
       if (bytes) {
         if (lane == 0)
-          bulk_g2s(dst, reinterpret_cast<const uint8_t*>(p.scales) + a0, bytes, &meta_full[i & 1],
+          bulk_g2s(dst, reinterpret_cast<const uint8_t*>(p.scales) + a0, bytes, &meta_full[mb],
                    pol_x);
         if (!SYM && lane == 1)
           bulk_g2s(dst + p.meta_half, reinterpret_cast<const uint8_t*>(p.zeros) + a0, bytes,
-                   &meta_full[i & 1], pol_x);
+                   &meta_full[mb], pol_x);
       }
     };
     auto issue_stage = [&](int s) {
@@ -306,8 +307,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                  &full[slot], pol_w);
     };
     // Weights and metadata do not depend on the previous grid; activations
-    // may. Metadata buffers hold two tiles, so at most two tiles go ahead.
-    const int pre = min(min(S, total), 2 * p.n_slabs);
+    // may. NMB metadata buffers: at most NMB tiles go ahead.
+    const int pre = min(min(S, total), NMB * p.n_slabs);
     for (int s = 0; s < pre; ++s) issue_stage(s);
     pdl_wait_prior_grid();
     if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * p.K * 2);
@@ -320,10 +321,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const int slot = s % S;
       if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) break;
       const int i = s / p.n_slabs;
-      if (i >= 2 && s == i * p.n_slabs) {
-        // Metadata buffer (i & 1) is free once tile i - 2 is consumed: its
+      if (i >= NMB && s == i * p.n_slabs) {
+        // Metadata buffer i % NMB is free once tile i - NMB is consumed: its
         // last stage t released (implied by the wait above when t <= s - S).
-        const int t = (i - 1) * p.n_slabs - 1;
+        const int t = (i - NMB + 1) * p.n_slabs - 1;
         if (t > s - S && !warp_wait(&empty[t % S], (t / S) & 1)) break;
       }
       issue_stage(s);
@@ -331,8 +332,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // Drain: every copy this warp issued has landed before the CTA exits.
     for (int t = max(0, s - S); t < s; ++t) mbar_wait(&full[t % S], (t / S) & 1);
     const int issued_tiles = (s + p.n_slabs - 1) / p.n_slabs;
-    for (int ii = max(0, issued_tiles - 2); ii < issued_tiles; ++ii)
-      mbar_wait(&meta_full[ii & 1], (ii >> 1) & 1);
+    for (int ii = max(0, issued_tiles - NMB); ii < issued_tiles; ++ii)
+      mbar_wait(&meta_full[ii % NMB], (ii / NMB) & 1);
     mbar_wait(x_full, 0);
   } else if (warp == 1) {
     // ------------------------------------------------------------- reducer
@@ -497,8 +498,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const int r0 = row_begin + i * kTile;
       // (Waited for in every mode: the producer reuses a metadata buffer
       // only after its previous copy has been seen complete here.)
-      if (!warp_wait(&meta_full[i & 1], (i >> 1) & 1)) return;
-      const uint8_t* meta = smem + p.off_meta + (i & 1) * p.meta_stride;
+      if (!warp_wait(&meta_full[i % NMB], (i / NMB) & 1)) return;
+      const uint8_t* meta = smem + p.off_meta + (i % NMB) * p.meta_stride;
       const int64_t a0 = (static_cast<int64_t>(r0) * p.G * 2) & ~15ll;
       // Byte offsets of (row gid, group 0) and (row gid + 8, group 0).
       const int mo_a = static_cast<int>(static_cast<int64_t>(r0 + gid) * p.G * 2 - a0);
@@ -691,18 +692,16 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   off += round_up(M * (K / sc) * 4, 128);
   pl.off_sx = off;
   off += round_up(M * G * 4, 128);
-  // Metadata: two tile buffers, each [scales span | zeros span] of 16 rows x G
-  // fp16 plus up to 16 bytes of alignment slack.
+  // Metadata: a ring of tile buffers, each [scales span | zeros span] of 16
+  // rows x G fp16 plus up to 16 bytes of alignment slack.
   pl.meta_half = round_up(kTile * G * 2 + 32, 128);
   pl.meta_stride = 2 * pl.meta_half;
-  pl.off_meta = off;
-  off += 2 * pl.meta_stride;
   pl.off_red = off;
   off += round_up(kStreamNRB * kStreamNCW * kTile * M * 4, 128);
   pl.off_bar = off;
-  off += kBarBytes;
-  if (off > kStreamMaxFixedBytes) return false;
-  const int ring_base = round_up(off, 128);
+  off += kStreamBarBytes;
+  pl.off_meta = off;  // NMB tile metadata buffers follow
+  if (off + 2 * pl.meta_stride > kStreamMaxFixedBytes) return false;
   // Slabs: about kStreamStageBytes of packed weights per 16-row stage, in
   // whole consumer units.
   const int64_t row_bytes = static_cast<int64_t>(K) * bits / 8;
@@ -715,10 +714,19 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   pl.n_slabs = n_slabs;
   pl.w_pitch = round_up(ks * bits / 8, 128) + 16 * wpl;
   pl.stage_bytes = round_up(kTile * pl.w_pitch, 128);
-  int stages = (kMaxSmemBytes - ring_base) / pl.stage_bytes;
+  // Ring stages with two metadata buffers first; then more metadata buffers
+  // (one per tile the ring can hold, plus one) while they fit.
+  int stages = (kMaxSmemBytes - off - 2 * pl.meta_stride) / pl.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
+  int n_meta = (stages + n_slabs - 1) / n_slabs + 1;
+  if (n_meta > kStreamMaxMeta) n_meta = kStreamMaxMeta;
+  while (n_meta > 2 && off + n_meta * pl.meta_stride + stages * pl.stage_bytes > kMaxSmemBytes)
+    --n_meta;
+  if (n_meta < 2) n_meta = 2;
   pl.stages = stages;
+  pl.n_meta = n_meta;
+  off += n_meta * pl.meta_stride;
   // The ring sits at offset 0; everything else follows it.
   const int ring = stages * pl.stage_bytes;
   pl.off_x += ring;
@@ -750,6 +758,7 @@ cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t 
   p.KS = pl.ks;
   p.n_slabs = pl.n_slabs;
   p.stages = pl.stages;
+  p.n_meta = pl.n_meta;
   p.w_pitch = pl.w_pitch;
   p.xp = pl.xp;
   p.stage_bytes = pl.stage_bytes;
