@@ -1,667 +1,23 @@
-// Fused low-bit dequantize + GEMV for B200 (sm_100a): the streaming kernel.
-//
-// y[m, n] = fp16( sum_k x[m, k] * (q[n, k] - off[n, k/g]) * scale[n, k/g] ),
-// fp32 accumulation, 1 <= M <= 8, packed format of the reference packer
-// (KrishnaI2424/Dequant_Project dequant/packer.py:7-29). It replaces the
-// reference kernel kernels/dequant_gemv.cu:144-217 whenever the activations
-// fit in shared memory.
-//
-// Design (one CTA per SM; rows balanced across CTAs to within one row):
-//   * warp 0 (producer) streams the CTA's rows as (16-row tile, K slab)
-//     stages into a ring of shared-memory slots: one bulk copy
-//     (cp.async.bulk, no multicast) per packed row segment, plus each tile's
-//     scales/zero-points as one contiguous span. Weights and metadata are
-//     issued before the programmatic-dependent-launch wait, activations after.
-//   * warps 2.. (consumers) first rewrite the resident activations in place
-//     into the tensor-core B-fragment order and take per-step sums; then, per
-//     stage, unpack codes in registers and run mma.m16n8k16 (fp16 x fp16 ->
-//     fp32) with 16 weight rows as the M side.
-//   * warp 1 (reducer) sums the consumer warps' partials of each tile in a
-//     fixed order and writes y.
-//
-// Exact unpack with compile-time constants: a code pair at bit position p of
-// the two 16-bit halves (p + bits <= 10) is dropped into the mantissa of fp16
-// 1024 by one LOP3 and centred by one HADD2 with -(1024 + c * 2^p), c =
-// 2^(bits - 1), giving (q - c) * 2^p exactly. A word yields its pairs at 1
-// (INT8), 2 (INT4) or 4 (INT2) positions p; each position accumulates in its
-// own MMA chain and the chains are combined in fp32 with exact power-of-two
-// factors. Centring keeps the tensor-core partial sums as small as in a
-// dequantized product. The offset is applied per group in fp32 through the
-// group's activation sum:
-//   sum_k (q - z) x = P - (z - c) * Sx,   P = sum_k (q - c) x,   Sx = sum_k x,
-// so any zero-point (fractional, out of range) is handled the same way, and the
-// scale multiplies the group's result in fp32 (as the reference kernel does per
-// chunk, dequant_gemv.cu:199-200).
-//
-// Group slots: the MMA's N=8 side holds mp activation rows (mp = M rounded up
-// to a power of two) times 8/mp consecutive groups; a lane's B fragment is
-// zero unless its column's group is the one being streamed, so one MMA chain
-// collects up to 8 group partials at once and their scale/offset work is
-// spread over all lanes (for M=1 this is 8x fewer scale instructions than one
-// group per chain).
+// Host side of the streaming GEMV kernel (gemv_stream.cuh): shared-memory
+// plan and launch. The kernel variants are instantiated per bit width in
+// gemv_stream_b{2,4,8}.cu so that they compile in parallel.
 #include <cstdint>
-#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
-#include "common.cuh"
 #include "gemv.h"
 
 namespace dqg {
 
+cudaError_t launch_stream_b2(int wpl, int gs, bool sym, bool inter, const StreamParams& p,
+                             int grid, int smem, cudaStream_t stream);
+cudaError_t launch_stream_b4(int wpl, int gs, bool sym, bool inter, const StreamParams& p,
+                             int grid, int smem, cudaStream_t stream);
+cudaError_t launch_stream_b8(int wpl, int gs, bool sym, bool inter, const StreamParams& p,
+                             int grid, int smem, cudaStream_t stream);
+
 namespace {
 
-// B-fragment register r of a word holds the activations of slots
-// (b_slot(r, 0), b_slot(r, 1)); unpack_sub produces the code pairs of the same
-// slots in the same order.
-__host__ __device__ constexpr int b_slot(int bits, int r, int hi) {
-  if (bits == 4) return (r == 0 ? 0 : r == 1 ? 2 : r == 2 ? 1 : 3) + (hi ? 4 : 0);
-  if (bits == 2) return (r >> 1) + ((r & 1) ? 4 : 0) + (hi ? 8 : 0);
-  return r + (hi ? 2 : 0);
-}
-
-// Bit position (within a 16-bit half) of the codes of MMA chain mi.
-__host__ __device__ constexpr int chain_pos(int bits, int mi) {
-  return bits == 4 ? 4 * mi : bits == 2 ? 2 * mi : 0;
-}
-
-// Code pairs of one word as centred fp16 integers (q - c) * 2^p, c =
-// 2^(bits - 1), in b_slot order: one LOP3 drops a pair into the mantissa of
-// 1024 (giving 1024 + q * 2^p exactly, p + bits <= 10) and one HADD2 with the
-// constant -(1024 + c * 2^p) leaves (q - c) * 2^p, exactly.
-template <int BITS>
-__device__ __forceinline__ void unpack_centered(uint32_t w, uint32_t* pa) {
-  constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
-  if constexpr (BITS == 4) {
-    const uint32_t w8 = prmt(w, 0u, 0x4341u);  // (w >> 8) & 0x00FF00FF
-    pa[0] = hadd2_u32(lop3_and_or(w, 0x000F000Fu, kMagic), 0xE408E408u);   // slots 0, 4 (p = 0)
-    pa[1] = hadd2_u32(lop3_and_or(w8, 0x000F000Fu, kMagic), 0xE408E408u);  // slots 2, 6 (p = 0)
-    pa[2] = hadd2_u32(lop3_and_or(w, 0x00F000F0u, kMagic), 0xE480E480u);   // slots 1, 5 (p = 4)
-    pa[3] = hadd2_u32(lop3_and_or(w8, 0x00F000F0u, kMagic), 0xE480E480u);  // slots 3, 7 (p = 4)
-  } else if constexpr (BITS == 2) {
-    const uint32_t w8 = prmt(w, 0u, 0x4341u);
-    constexpr uint32_t kc[4] = {0xE402E402u, 0xE408E408u, 0xE420E420u, 0xE480E480u};
-#pragma unroll
-    for (int f = 0; f < 4; ++f) {
-      pa[2 * f] = hadd2_u32(lop3_and_or(w, 0x00030003u << (2 * f), kMagic), kc[f]);   // f, f + 8
-      pa[2 * f + 1] = hadd2_u32(lop3_and_or(w8, 0x00030003u << (2 * f), kMagic), kc[f]);  // f + 4, f + 12
-    }
-  } else {
-    pa[0] = hadd2_u32(prmt(w, kMagic, 0x7250u), 0xE480E480u);  // slots 0, 2
-    pa[1] = hadd2_u32(prmt(w, kMagic, 0x7351u), 0xE480E480u);  // slots 1, 3
-  }
-}
-
-__device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-template <int NB>
-__device__ __forceinline__ void lds(const uint8_t* p, uint32_t* r) {
-  if constexpr (NB == 4) {
-    r[0] = *reinterpret_cast<const uint32_t*>(p);
-  } else if constexpr (NB == 8) {
-    const uint2 v = *reinterpret_cast<const uint2*>(p);
-    r[0] = v.x;
-    r[1] = v.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < NB / 16; ++i) {
-      const uint4 v = *reinterpret_cast<const uint4*>(p + 16 * i);
-      r[4 * i + 0] = v.x;
-      r[4 * i + 1] = v.y;
-      r[4 * i + 2] = v.z;
-      r[4 * i + 3] = v.w;
-    }
-  }
-}
-
-template <int NB>
-__device__ __forceinline__ void sts(uint8_t* p, const uint32_t* r) {
-  if constexpr (NB == 8) {
-    *reinterpret_cast<uint2*>(p) = make_uint2(r[0], r[1]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < NB / 16; ++i)
-      *reinterpret_cast<uint4*>(p + 16 * i) =
-          make_uint4(r[4 * i + 0], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-  }
-}
-
-// Shared-memory layout of a step's activations (B-fragment order): lane c's
-// LXB bytes are cut into U-byte units; unit u of lane c sits at u * 4U + c * U,
-// so the four lanes of a fragment row read one contiguous 4U-byte run.
-template <int BITS, int WPL>
-struct XUnits {
-  static constexpr int WB = 64 / BITS;          // activation bytes per word
-  static constexpr int LXB = WPL * WB;          // per lane per step
-  static constexpr int U = LXB >= 16 ? 16 : LXB;
-  static constexpr int NU = LXB / U;
-};
-
-// One step of one lane: WPL words of rows gid and gid + 8 and their
-// activations (loaded only when this lane's fragment column is live; zero
-// otherwise), NF MMAs per word into chain set j % NSET.
-template <int BITS, int WPL, int NSET>
-__device__ __forceinline__ void mma_step(const uint8_t* pa, const uint8_t* pb, const uint8_t* px,
-                                         bool live, float (&D)[NSET][(16 / BITS) / 2][4]) {
-  constexpr int NPAIR = 16 / BITS;
-  constexpr int NF = NPAIR / 2;
-  using XU = XUnits<BITS, WPL>;
-  uint32_t wa[WPL], wb[WPL];
-  lds<WPL * 4>(pa, wa);
-  lds<WPL * 4>(pb, wb);
-  uint32_t bx[WPL * NPAIR];
-  if (live) {
-#pragma unroll
-    for (int u = 0; u < XU::NU; ++u) lds<XU::U>(px + u * 4 * XU::U, bx + u * (XU::U / 4));
-  } else {
-#pragma unroll
-    for (int r = 0; r < WPL * NPAIR; ++r) bx[r] = 0u;
-  }
-#pragma unroll
-  for (int j = 0; j < WPL; ++j) {
-    uint32_t ua[NPAIR], ub[NPAIR];
-    unpack_centered<BITS>(wa[j], ua);
-    unpack_centered<BITS>(wb[j], ub);
-#pragma unroll
-    for (int mi = 0; mi < NF; ++mi)
-      mma16816(D[j % NSET][mi], ua[2 * mi], ub[2 * mi], ua[2 * mi + 1], ub[2 * mi + 1],
-               bx[j * NPAIR + 2 * mi], bx[j * NPAIR + 2 * mi + 1]);
-  }
-}
-
-// sum_k (q - c) x of each accumulator element: chains combined with their
-// exact power-of-two factors.
-template <int BITS, int NSET>
-__device__ __forceinline__ void combine(float (&D)[NSET][(16 / BITS) / 2][4], float* P) {
-  constexpr int NF = (16 / BITS) / 2;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    float v = D[0][0][e];
-#pragma unroll
-    for (int set = 1; set < NSET; ++set) v += D[set][0][e];
-#pragma unroll
-    for (int mi = 1; mi < NF; ++mi) {
-      const float f = 1.0f / static_cast<float>(1 << chain_pos(BITS, mi));
-#pragma unroll
-      for (int set = 0; set < NSET; ++set) v = fmaf(D[set][mi][e], f, v);
-    }
-    P[e] = v;
-  }
-}
-
-template <int BITS, bool SYM, bool INTER, int WPL, bool GROUPED>
-__global__ void __launch_bounds__(kStreamThreads, 1)
-    gemv_stream_kernel(const __grid_constant__ StreamParams p) {
-  constexpr int PP = 32 / BITS;         // codes per word
-  constexpr int NPAIR = PP / 2;         // B registers per word
-  constexpr int NF = NPAIR / 2;         // MMA chains per word (code positions)
-  constexpr int SC = 4 * WPL * PP;      // codes per step
-  constexpr int WB = PP * 2;            // activation bytes per word
-  constexpr int LXB = WPL * WB;         // activation bytes per lane per step
-  constexpr int STEP_XB = SC * 2;       // activation bytes per step
-  constexpr int SW = 4 * WPL;           // words per step
-  constexpr int NSET = WPL >= 2 ? 2 : 1;
-  constexpr float kBias = static_cast<float>(1 << (BITS - 1));
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* meta_full = empty + kMaxStages;     // [kStreamMaxMeta]
-  uint64_t* red_full = meta_full + kStreamMaxMeta;  // [kStreamNRB]
-  uint64_t* red_empty = red_full + kStreamNRB;  // [kStreamNRB]
-  uint64_t* x_full = red_empty + kStreamNRB;
-  uint64_t* pro_bar = x_full + 1;               // [2] consumer prologue barriers
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int S = p.stages;
-  const int NMB = p.n_meta;
-  const int64_t row_bytes = static_cast<int64_t>(p.K) * BITS / 8;
-  const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
-  const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
-  const int n_tiles = (row_end - row_begin + kTile - 1) / kTile;
-  const int total = n_tiles * p.n_slabs;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kStreamNCW);
-    }
-    for (int b = 0; b < NMB; ++b) mbar_init(&meta_full[b], 1);
-    for (int b = 0; b < kStreamNRB; ++b) {
-      mbar_init(&red_full[b], kStreamNCW);
-      mbar_init(&red_empty[b], 1);
-    }
-    mbar_init(x_full, 1);
-    mbar_init(&pro_bar[0], kStreamNCW);
-    mbar_init(&pro_bar[1], kStreamNCW);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) pdl_launch_dependents();
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    const uint64_t pol_w = policy_evict_first();
-    const uint64_t pol_x = policy_evict_last();
-    const uint8_t* qw = reinterpret_cast<const uint8_t*>(p.qw);
-    // The last few scales/zeros elements past the tensors' last 16-byte
-    // boundary cannot be bulk-copied; the last CTA reads them here and stores
-    // them into its final tile's metadata buffer.
-    uint16_t tail_s = 0, tail_z = 0;
-    if (blockIdx.x == gridDim.x - 1 && lane < p.tail_n) {
-      tail_s = p.scales[p.tail_first + lane];
-      if (!SYM) tail_z = p.zeros[p.tail_first + lane];
-    }
-    // A tile's scales (and zeros): rows [r0, r0 + R) x all groups, one
-    // contiguous span, copied from its enclosing 16-byte boundary a0.
-    auto issue_meta = [&](int i) {
-      const int r0 = row_begin + i * kTile;
-      const int R = min(kTile, row_end - r0);
-      const int64_t e0 = static_cast<int64_t>(r0) * p.G;
-      const int64_t e1 = static_cast<int64_t>(r0 + R) * p.G;
-      const int64_t a0 = (e0 * 2) & ~15ll;
-      const int64_t a1 = min((e1 * 2 + 15) & ~15ll, p.tail_first * 2);
-      const uint32_t bytes = a1 > a0 ? static_cast<uint32_t>(a1 - a0) : 0u;
-      const int mb = i % NMB;
-      uint8_t* dst = smem + p.off_meta + mb * p.meta_stride;
-      if (e1 > p.tail_first) {
-        const int64_t e = p.tail_first + lane;
-        if (lane < p.tail_n && e >= e0 && e < e1) {
-          *reinterpret_cast<uint16_t*>(dst + e * 2 - a0) = tail_s;
-          if (!SYM) *reinterpret_cast<uint16_t*>(dst + p.meta_half + e * 2 - a0) = tail_z;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(&meta_full[mb], SYM ? bytes : 2 * bytes);
-      __syncwarp();
-      if (bytes) {
-        if (lane == 0)
-          bulk_g2s(dst, reinterpret_cast<const uint8_t*>(p.scales) + a0, bytes, &meta_full[mb],
-                   pol_x);
-        if (!SYM && lane == 1)
-          bulk_g2s(dst + p.meta_half, reinterpret_cast<const uint8_t*>(p.zeros) + a0, bytes,
-                   &meta_full[mb], pol_x);
-      }
-    };
-    auto issue_stage = [&](int s) {
-      const int i = s / p.n_slabs, j = s - (s / p.n_slabs) * p.n_slabs;
-      const int r0 = row_begin + i * kTile;
-      const int R = min(kTile, row_end - r0);
-      const int k0 = j * p.KS;
-      const int L = min(p.KS, p.K - k0);
-      const uint32_t run = static_cast<uint32_t>(L) * BITS / 8;
-      const int slot = s % S;
-      uint8_t* st = smem + slot * p.stage_bytes;
-      if (j == 0) issue_meta(i);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], R * run);
-      __syncwarp();
-      if (lane < R)
-        bulk_g2s(st + lane * p.w_pitch, qw + (r0 + lane) * row_bytes + k0 * BITS / 8, run,
-                 &full[slot], pol_w);
-    };
-    // Weights and metadata do not depend on the previous grid; activations
-    // may. NMB metadata buffers: at most NMB tiles go ahead.
-    const int pre = min(min(S, total), NMB * p.n_slabs);
-    for (int s = 0; s < pre; ++s) issue_stage(s);
-    pdl_wait_prior_grid();
-    if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * p.K * 2);
-    __syncwarp();
-    if (lane < p.M)
-      bulk_g2s(smem + p.off_x + lane * p.xp, p.x + static_cast<int64_t>(lane) * p.K,
-               static_cast<uint32_t>(p.K) * 2, x_full, pol_x);
-    int s = pre;
-    for (; s < total; ++s) {
-      const int slot = s % S;
-      if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) break;
-      const int i = s / p.n_slabs;
-      if (i >= NMB && s == i * p.n_slabs) {
-        // Metadata buffer i % NMB is free once tile i - NMB is consumed: its
-        // last stage t released (implied by the wait above when t <= s - S).
-        const int t = (i - NMB + 1) * p.n_slabs - 1;
-        if (t > s - S && !warp_wait(&empty[t % S], (t / S) & 1)) break;
-      }
-      issue_stage(s);
-    }
-    // Drain: every copy this warp issued has landed before the CTA exits.
-    for (int t = max(0, s - S); t < s; ++t) mbar_wait(&full[t % S], (t / S) & 1);
-    const int issued_tiles = (s + p.n_slabs - 1) / p.n_slabs;
-    for (int ii = max(0, issued_tiles - NMB); ii < issued_tiles; ++ii)
-      mbar_wait(&meta_full[ii % NMB], (ii / NMB) & 1);
-    mbar_wait(x_full, 0);
-  } else if (warp == 1) {
-    // ------------------------------------------------------------- reducer
-    const float* sxg = reinterpret_cast<const float*>(smem + p.off_sx);
-    for (int i = 0; i < n_tiles; ++i) {
-      const int b = i % kStreamNRB;
-      const int r0 = row_begin + i * kTile;
-      const int R = min(kTile, row_end - r0);
-      float sc = 0.f, zc = 0.f;
-      if constexpr (!GROUPED) {
-        // Per-channel: one scale (and zero) per row, applied here.
-        if (lane < R) {
-          sc = __half2float(__ushort_as_half(p.scales[r0 + lane]));
-          zc = SYM ? kBias : __half2float(__ushort_as_half(p.zeros[r0 + lane]));
-        }
-      }
-      if (!warp_wait(&red_full[b], (i / kStreamNRB) & 1)) return;
-      if constexpr (!GROUPED) {
-        if (!warp_wait(&pro_bar[1], 0)) return;
-      }
-      const float* red = reinterpret_cast<const float*>(smem + p.off_red) +
-                         b * (kStreamNCW * kTile * p.M);
-      for (int idx0 = 0; idx0 < kTile * p.M; idx0 += 32) {
-        const int idx = idx0 + lane;
-        const int row = idx & (kTile - 1);
-        const int m = idx >> 4;
-        const float s_row = __shfl_sync(0xffffffffu, sc, row);
-        const float z_row = __shfl_sync(0xffffffffu, zc, row);
-        if (idx < kTile * p.M && row < R) {
-          float sum = 0.f;
-#pragma unroll
-          for (int w = 0; w < kStreamNCW; ++w) sum += red[(w * kTile + row) * p.M + m];
-          if constexpr (!GROUPED) sum = s_row * (SYM ? sum : fmaf(-(z_row - kBias), sxg[m], sum));
-          p.y[static_cast<int64_t>(m) * p.N + r0 + row] =
-              __half_as_ushort(__float2half_rn(sum));
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&red_empty[b]);
-    }
-  } else {
-    // ----------------------------------------------------------- consumers
-    using XU = XUnits<BITS, WPL>;
-    const int cw = warp - 2;
-    const int tid = cw * 32 + lane;
-    constexpr int kCT = kStreamNCW * 32;
-    float* sstep = reinterpret_cast<float*>(smem + p.off_sstep);
-    float* sxg = reinterpret_cast<float*>(smem + p.off_sx);
-    const int spr = p.K / SC;  // steps per activation row
-
-    // Prologue 1: activations, in place, into B-fragment order, with per-step
-    // sums. One word per lane; a step's SW words are all in this warp, so
-    // every lane has loaded its word before any lane overwrites the step.
-    if (!warp_wait(x_full, 0)) return;
-    {
-      const int wpr = p.K / PP;
-      const int nwords = p.M * wpr;
-      for (int w0 = cw * 32; w0 < nwords; w0 += kCT) {
-        const int w = w0 + lane;
-        const bool have = w < nwords;
-        const int m = have ? w / wpr : 0;
-        const int wi = w - m * wpr;
-        uint8_t* row = smem + p.off_x + m * p.xp;
-        uint32_t v[NPAIR];
-        float sum = 0.f;
-        if (have) {
-          lds<WB>(row + wi * WB, v);
-          // Pairwise sum of the word's activations.
-          float f[PP];
-#pragma unroll
-          for (int q = 0; q < NPAIR; ++q) {
-            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&v[q]));
-            f[2 * q] = t.x;
-            f[2 * q + 1] = t.y;
-          }
-#pragma unroll
-          for (int h = PP / 2; h >= 1; h >>= 1)
-#pragma unroll
-            for (int q = 0; q < h; ++q) f[q] += f[q + h];
-          sum = f[0];
-        }
-        __syncwarp();
-        if (have) {
-          uint32_t o[NPAIR];
-#pragma unroll
-          for (int r = 0; r < NPAIR; ++r) {
-            const int lo = slot_logical(BITS, INTER, b_slot(BITS, r, 0));
-            const int hi = slot_logical(BITS, INTER, b_slot(BITS, r, 1));
-            o[r] = prmt(v[lo >> 1], v[hi >> 1],
-                        ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
-          }
-          const int st = wi / SW;
-          const int q = wi - st * SW;
-          const int cc = q / WPL;
-          const int j = q - cc * WPL;
-          constexpr int PB = WB < XU::U ? WB : XU::U;
-          uint8_t* sbase = row + st * STEP_XB + cc * XU::U;
-#pragma unroll
-          for (int pc = 0; pc < WB / PB; ++pc) {
-            const int lb = j * WB + pc * PB;
-            sts<PB>(sbase + (lb / XU::U) * 4 * XU::U + (lb % XU::U), o + pc * (PB / 4));
-          }
-        }
-        // Steps are SW consecutive words and never straddle rows.
-#pragma unroll
-        for (int off = SW / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        if ((lane & (SW - 1)) == 0 && have) sstep[m * spr + wi / SW] = sum;
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pro_bar[0]);
-    if (!warp_wait(&pro_bar[0], 0)) return;
-    // Prologue 2: the activation sum of every group (per-channel: of the
-    // whole row).
-    if constexpr (GROUPED) {
-      const int spg = p.gsize / SC;
-      for (int e = tid; e < p.M * p.G; e += kCT) {
-        const int m = e / p.G;
-        const int g = e - m * p.G;
-        const float* src = sstep + m * spr + g * spg;
-        float sum = 0.f;
-        for (int t = 0; t < spg; ++t) sum += src[t];
-        sxg[e] = sum;
-      }
-    } else {
-      if (cw < p.M) {
-        float sum = 0.f;
-        for (int t = lane; t < spr; t += 32) sum += sstep[cw * spr + t];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        if (lane == 0) sxg[cw] = sum;
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pro_bar[1]);
-    if (!warp_wait(&pro_bar[1], 0)) return;
-
-    // Main loop. Work units (grouped: gslots consecutive groups; per-channel:
-    // one step) go to warps round-robin by their index over the whole CTA.
-    const int gid = lane >> 2;
-    const int c = lane & 3;
-    const int mp = p.mp;
-    const int gslots = 8 / mp;
-    const int my_slot = gid / mp;
-    const int my_xrow = gid - my_slot * mp;
-    const bool x_ok = my_xrow < p.M;
-    const uint8_t* xrow_base = smem + p.off_x + (x_ok ? my_xrow : 0) * p.xp + c * XU::U;
-    constexpr int kStepWB = SC * BITS / 8;  // packed bytes per step per row
-    const int spg = p.gsize / SC;
-    const int units_per_tile = GROUPED ? (p.G + gslots - 1) / gslots : spr;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float D[NSET][NF][4];
-#pragma unroll
-    for (int set = 0; set < NSET; ++set)
-#pragma unroll
-      for (int mi = 0; mi < NF; ++mi)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
-
-    int s = 0;
-    for (int i = 0; i < n_tiles; ++i) {
-      const int r0 = row_begin + i * kTile;
-      // (Waited for in every mode: the producer reuses a metadata buffer
-      // only after its previous copy has been seen complete here.)
-      if (!warp_wait(&meta_full[i % NMB], (i / NMB) & 1)) return;
-      const uint8_t* meta = smem + p.off_meta + (i % NMB) * p.meta_stride;
-      const int64_t a0 = (static_cast<int64_t>(r0) * p.G * 2) & ~15ll;
-      // Byte offsets of (row gid, group 0) and (row gid + 8, group 0).
-      const int mo_a = static_cast<int>(static_cast<int64_t>(r0 + gid) * p.G * 2 - a0);
-      const int mo_b = mo_a + 8 * p.G * 2;
-      for (int j = 0; j < p.n_slabs; ++j, ++s) {
-        const int slot = s % S;
-        if (!warp_wait(&full[slot], (s / S) & 1)) return;
-        const int k0 = j * p.KS;
-        const int L = min(p.KS, p.K - k0);
-        const uint8_t* st = smem + slot * p.stage_bytes;
-        const uint8_t* wa_row = st + gid * p.w_pitch + c * WPL * 4;
-        const uint8_t* wb_row = wa_row + 8 * p.w_pitch;
-        if constexpr (GROUPED) {
-          const int g_slab = k0 / p.gsize;
-          const int ng = L / p.gsize;
-          const int units = (ng + gslots - 1) / gslots;
-          const int ubase = i * units_per_tile + g_slab / gslots;
-          for (int u = (cw - ubase % kStreamNCW + kStreamNCW) % kStreamNCW; u < units;
-               u += kStreamNCW) {
-#pragma unroll
-            for (int set = 0; set < NSET; ++set)
-#pragma unroll
-              for (int mi = 0; mi < NF; ++mi)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
-            for (int gs = 0; gs < gslots; ++gs) {
-              const int gl = u * gslots + gs;
-              if (gl >= ng) break;
-              const bool live = x_ok && my_slot == gs;
-              const int st0 = gl * spg;         // first step of the group in the slab
-              const int kst = k0 / SC + st0;    // its step index along K
-              for (int t = 0; t < spg; ++t) {
-                const int wofs = (st0 + t) * kStepWB;
-                mma_step<BITS, WPL, NSET>(wa_row + wofs, wb_row + wofs,
-                                          xrow_base + (kst + t) * STEP_XB, live, D);
-              }
-            }
-            float P[4];
-            combine<BITS, NSET>(D, P);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int col = 2 * c + (e & 1);
-              const int slot_e = col / mp;
-              const int xrow = col - slot_e * mp;
-              const int gl = u * gslots + slot_e;
-              if (gl < ng && xrow < p.M) {
-                const int g = g_slab + gl;
-                const int mo = ((e >> 1) ? mo_b : mo_a) + g * 2;
-                const float sv = __half2float(*reinterpret_cast<const __half*>(meta + mo));
-                float t = P[e];
-                if constexpr (!SYM) {
-                  const float zv =
-                      __half2float(*reinterpret_cast<const __half*>(meta + p.meta_half + mo));
-                  t = fmaf(-(zv - kBias), sxg[xrow * p.G + g], t);
-                }
-                acc[e] = fmaf(sv, t, acc[e]);
-              }
-            }
-          }
-        } else {
-          const int steps = L / SC;
-          const int st_glob0 = k0 / SC;
-          const int ubase = i * units_per_tile + st_glob0;
-          for (int u = (cw - ubase % kStreamNCW + kStreamNCW) % kStreamNCW; u < steps;
-               u += kStreamNCW)
-            mma_step<BITS, WPL, NSET>(wa_row + u * kStepWB, wb_row + u * kStepWB,
-                                      xrow_base + (st_glob0 + u) * STEP_XB, x_ok, D);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-      }
-
-      // Tile end: per (row, activation row) partial of this warp.
-      if constexpr (!GROUPED) {
-        combine<BITS, NSET>(D, acc);
-#pragma unroll
-        for (int set = 0; set < NSET; ++set)
-#pragma unroll
-          for (int mi = 0; mi < NF; ++mi)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
-      }
-      // Columns sharing an activation row (different group slots) are summed
-      // across lanes: slots are the high bits of the column 2c + (e & 1).
-      if (mp == 1) {
-        acc[0] += acc[1];
-        acc[2] += acc[3];
-      }
-      if (mp <= 2) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 1);
-          acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 2);
-        }
-      } else if (mp == 4) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 2);
-      }
-      const int b = i % kStreamNRB;
-      if (i >= kStreamNRB && !warp_wait(&red_empty[b], ((i / kStreamNRB) - 1) & 1)) return;
-      float* red = reinterpret_cast<float*>(smem + p.off_red) + b * (kStreamNCW * kTile * p.M) +
-                   cw * kTile * p.M;
-      const int cmask = mp <= 2 ? 3 : (mp == 4 ? 2 : 0);
-      if ((c & cmask) == 0) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (mp == 1 && (e & 1)) continue;
-          const int row = gid + 8 * (e >> 1);
-          const int xrow = (2 * c + (e & 1)) & (mp - 1);
-          if (xrow < p.M) red[row * p.M + xrow] = acc[e];
-        }
-      }
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&red_full[b]);
-    }
-  }
-}
-
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
-
-template <int BITS, bool SYM, bool INTER, int WPL, bool GROUPED>
-cudaError_t launch_variant(const StreamParams& p, int grid, int smem, cudaStream_t stream) {
-  auto kern = gemv_stream_kernel<BITS, SYM, INTER, WPL, GROUPED>;
-  static int configured[64] = {0};  // max dynamic smem already raised, per device
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemBytes);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev] = 1;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kStreamThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
-}
-
-template <int BITS, bool SYM, bool INTER, int WPL>
-cudaError_t dispatch_grouped(bool grouped, const StreamParams& p, int grid, int smem,
-                             cudaStream_t stream) {
-  return grouped ? launch_variant<BITS, SYM, INTER, WPL, true>(p, grid, smem, stream)
-                 : launch_variant<BITS, SYM, INTER, WPL, false>(p, grid, smem, stream);
-}
-
-template <int BITS, bool SYM, bool INTER>
-cudaError_t dispatch_wpl(int wpl, bool grouped, const StreamParams& p, int grid, int smem,
-                         cudaStream_t stream) {
-  switch (wpl) {
-    case 4: return dispatch_grouped<BITS, SYM, INTER, 4>(grouped, p, grid, smem, stream);
-    case 2: return dispatch_grouped<BITS, SYM, INTER, 2>(grouped, p, grid, smem, stream);
-    default: return dispatch_grouped<BITS, SYM, INTER, 1>(grouped, p, grid, smem, stream);
-  }
-}
 
 }  // namespace
 
@@ -672,7 +28,10 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   const int sc = 4 * wpl * pp;
   const int G = K / group_size;
   const bool grouped = G > 1;
-  int mp = 1;
+  // Activation-row columns per group slot: M rounded up to a power of two,
+  // at least 2 (units of at most 4 groups keep every consumer warp busy on
+  // a 40 KB stage); per-channel: all 8 columns are activation rows.
+  int mp = 2;
   while (mp < M) mp <<= 1;
   if (!grouped) mp = 8;
   const int gslots = 8 / mp;
@@ -777,24 +136,13 @@ cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t 
   if (reinterpret_cast<uintptr_t>(a.scales) % 16 ||
       (a.zeros != nullptr && reinterpret_cast<uintptr_t>(a.zeros) % 16))
     return cudaErrorInvalidValue;
-  const bool grouped = p.G > 1;
-#define DQG_STREAM_CASE(B, S, I) \
-  if (a.bits == B && a.symmetric == S && a.interleaved == I) \
-    return dispatch_wpl<B, S, I>(pl.wpl, grouped, p, pl.grid, pl.smem, stream);
-  DQG_STREAM_CASE(2, false, false)
-  DQG_STREAM_CASE(2, false, true)
-  DQG_STREAM_CASE(2, true, false)
-  DQG_STREAM_CASE(2, true, true)
-  DQG_STREAM_CASE(4, false, false)
-  DQG_STREAM_CASE(4, false, true)
-  DQG_STREAM_CASE(4, true, false)
-  DQG_STREAM_CASE(4, true, true)
-  DQG_STREAM_CASE(8, false, false)
-  DQG_STREAM_CASE(8, false, true)
-  DQG_STREAM_CASE(8, true, false)
-  DQG_STREAM_CASE(8, true, true)
-#undef DQG_STREAM_CASE
-  return cudaErrorInvalidValue;
+  const int gs = p.G > 1 ? 8 / pl.mp : 0;
+  switch (a.bits) {
+    case 2: return launch_stream_b2(pl.wpl, gs, a.symmetric, a.interleaved, p, pl.grid, pl.smem, stream);
+    case 4: return launch_stream_b4(pl.wpl, gs, a.symmetric, a.interleaved, p, pl.grid, pl.smem, stream);
+    case 8: return launch_stream_b8(pl.wpl, gs, a.symmetric, a.interleaved, p, pl.grid, pl.smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace dqg
