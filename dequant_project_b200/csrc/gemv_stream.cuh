@@ -91,9 +91,11 @@ __device__ __forceinline__ void unpack_centered(uint32_t w, uint32_t* pa) {
   }
 }
 
+// Not volatile: a pure function of its operands, so the compiler may schedule
+// loads and unpacking of later steps around it.
 __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -207,7 +209,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   constexpr int NF = NPAIR / 2;         // MMA chains per word (code positions)
   constexpr int SC = 4 * WPL * PP;      // codes per step
   constexpr int WB = PP * 2;            // activation bytes per word
-  constexpr int LXB = WPL * WB;         // activation bytes per lane per step
   constexpr int STEP_XB = SC * 2;       // activation bytes per step
   constexpr int SW = 4 * WPL;           // words per step
   constexpr int NSET = WPL >= 2 ? 2 : 1;
@@ -311,8 +312,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                  &full[slot], pol_w);
     };
     // Weights and metadata do not depend on the previous grid; activations
-    // may. NMB metadata buffers: at most NMB tiles go ahead.
-    const int pre = min(min(S, total), NMB * p.n_slabs);
+    // may. Only the first stage goes ahead of the wait: the activations'
+    // copy would otherwise queue behind a ring's worth of weight copies, and
+    // nothing can be computed until it lands.
+    const int pre = min(1, total);
     for (int s = 0; s < pre; ++s) issue_stage(s);
     pdl_wait_prior_grid();
     if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * p.K * 2);
@@ -534,6 +537,28 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
               for (int mi = 0; mi < NF; ++mi)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
+            // This unit's scales, zero-points and activation sums, loaded
+            // before its MMAs.
+            bool ev[4];
+            float sv[4], zv[4], sxv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int col = 2 * c + (e & 1);
+              const int slot_e = col / mp;
+              const int xrow = col - slot_e * mp;
+              const int gl = u * gslots + slot_e;
+              ev[e] = gl < ng && xrow < p.M;
+              const int g = g_slab + (ev[e] ? gl : 0);
+              const int mo = ((e >> 1) ? mo_b : mo_a) + g * 2;
+              sv[e] = __half2float(*reinterpret_cast<const __half*>(meta + mo));
+              if constexpr (!SYM) {
+                zv[e] = __half2float(*reinterpret_cast<const __half*>(meta + p.meta_half + mo));
+                sxv[e] = sxg[(ev[e] ? xrow : 0) * p.G + g];
+              } else {
+                zv[e] = 0.f;
+                sxv[e] = 0.f;
+              }
+            }
             if (spg == 1 && (u + 1) * gslots <= ng) {
               // A whole unit of one-step groups: fully unrolled.
               const int st0 = u * gslots;
@@ -562,21 +587,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             combine<BITS, NSET>(D, P);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const int col = 2 * c + (e & 1);
-              const int slot_e = col / mp;
-              const int xrow = col - slot_e * mp;
-              const int gl = u * gslots + slot_e;
-              if (gl < ng && xrow < p.M) {
-                const int g = g_slab + gl;
-                const int mo = ((e >> 1) ? mo_b : mo_a) + g * 2;
-                const float sv = __half2float(*reinterpret_cast<const __half*>(meta + mo));
+              if (ev[e]) {
                 float t = P[e];
-                if constexpr (!SYM) {
-                  const float zv =
-                      __half2float(*reinterpret_cast<const __half*>(meta + p.meta_half + mo));
-                  t = fmaf(-(zv - kBias), sxg[xrow * p.G + g], t);
-                }
-                acc[e] = fmaf(sv, t, acc[e]);
+                if constexpr (!SYM) t = fmaf(-(zv[e] - kBias), sxv[e], t);
+                acc[e] = fmaf(sv[e], t, acc[e]);
               }
             }
           }
