@@ -80,7 +80,7 @@ constexpr int kStreamNCW = 8;     // consumer (tensor-core) warps
 constexpr int kStreamThreads = 32 * (2 + kStreamNCW);  // + producer + reducer
 constexpr int kStreamNRB = 4;     // tile reduction buffers
 constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations
-constexpr int kStreamStageBytes = 40 * 1024;   // target packed bytes per stage
+constexpr int kStreamStageBytes = 64 * 1024;   // target packed bytes per stage (long row runs)
 constexpr int kStreamMaxFixedBytes = 128 * 1024;  // cap on everything but the ring
 constexpr int kStreamMaxMeta = 8;  // tile metadata buffers
 constexpr int kStreamBarBytes = 512;

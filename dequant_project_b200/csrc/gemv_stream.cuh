@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint64_t* red_full = meta_full + kStreamMaxMeta;  // [kStreamNRB]
   uint64_t* red_empty = red_full + kStreamNRB;  // [kStreamNRB]
   uint64_t* x_full = red_empty + kStreamNRB;
-  uint64_t* pro_bar = x_full + 1;               // [2] consumer prologue barriers
+  uint64_t* sx_ready = x_full + 1;              // activation sums written (reducer)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -244,8 +244,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       mbar_init(&red_empty[b], 1);
     }
     mbar_init(x_full, 1);
-    mbar_init(&pro_bar[0], kStreamNCW);
-    mbar_init(&pro_bar[1], kStreamNCW);
+    mbar_init(sx_ready, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -311,11 +310,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         bulk_g2s(st + lane * p.w_pitch, qw + (r0 + lane) * row_bytes + k0 * BITS / 8, run,
                  &full[slot], pol_w);
     };
-    // Weights and metadata do not depend on the previous grid; activations
-    // may. Only the first stage goes ahead of the wait: the activations'
-    // copy would otherwise queue behind a ring's worth of weight copies, and
-    // nothing can be computed until it lands.
-    const int pre = min(1, total);
+    // Weights and metadata do not depend on the previous grid, activations
+    // may; but nothing can be computed before the activations land, and their
+    // copy would queue behind any weight copies issued ahead of it. So the
+    // activations go first, right after the wait, then the ring.
+    const int pre = 0;
     for (int s = 0; s < pre; ++s) issue_stage(s);
     pdl_wait_prior_grid();
     if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * p.K * 2);
@@ -359,7 +358,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
       if (!warp_wait(&red_full[b], (i / kStreamNRB) & 1)) return;
       if constexpr (!GROUPED) {
-        if (!warp_wait(&pro_bar[1], 0)) return;
+        if (!warp_wait(sx_ready, 0)) return;
       }
       const float* red = reinterpret_cast<const float*>(smem + p.off_red) +
                          b * (kStreamNCW * kTile * p.M);
@@ -392,74 +391,89 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int spr = p.K / SC;  // steps per activation row
 
     // Prologue 1: activations, in place, into B-fragment order, with per-step
-    // sums (asymmetric formats only). One word per lane; a step's SW words
-    // are all in this warp, so every lane has loaded its word before any lane
-    // overwrites the step.
-    if (!warp_wait(x_full, 0)) return;
-    {
+    // sums (asymmetric formats only). One word per lane per chunk of 32; a
+    // step's SW words are all in one chunk, so every lane has loaded its words
+    // before any lane overwrites them. Four chunks per pass keep four
+    // independent load/convert/shuffle chains in flight.
+    // The consumer warps synchronise the prologue with a named barrier (id 1):
+    // every consumer warp reaches both barriers, also when its activation
+    // wait gave up, so that none is left waiting; such a warp returns after.
+    const bool x_ok_wait = warp_wait(x_full, 0);
+    if (x_ok_wait) {
+      constexpr int kU = 4;
       const int wpr = p.K / PP;
       for (int m = 0; m < p.M; ++m) {
         uint8_t* row = smem + p.off_x + m * p.xp;
-        for (int w0 = cw * 32; w0 < wpr; w0 += kCT) {
-          const int wi = w0 + lane;
-          const bool have = wi < wpr;
-          uint32_t v[NPAIR];
-          float sum = 0.f;
-          if (have) {
-            lds<WB>(row + wi * WB, v);
-            if constexpr (!SYM) {
-              // Pairwise sum of the word's activations.
-              float f[PP];
+        for (int w0 = cw * 32; w0 < wpr; w0 += kU * kCT) {
+          uint32_t v[kU][NPAIR];
+          float sum[kU];
 #pragma unroll
-              for (int q = 0; q < NPAIR; ++q) {
-                const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&v[q]));
-                f[2 * q] = t.x;
-                f[2 * q + 1] = t.y;
+          for (int uu = 0; uu < kU; ++uu) {
+            const int wi = w0 + uu * kCT + lane;
+            sum[uu] = 0.f;
+            if (wi < wpr) {
+              lds<WB>(row + wi * WB, v[uu]);
+              if constexpr (!SYM) {
+                float f[PP];
+#pragma unroll
+                for (int q = 0; q < NPAIR; ++q) {
+                  const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&v[uu][q]));
+                  f[2 * q] = t.x;
+                  f[2 * q + 1] = t.y;
+                }
+#pragma unroll
+                for (int h = PP / 2; h >= 1; h >>= 1)
+#pragma unroll
+                  for (int q = 0; q < h; ++q) f[q] += f[q + h];
+                sum[uu] = f[0];
               }
-#pragma unroll
-              for (int h = PP / 2; h >= 1; h >>= 1)
-#pragma unroll
-                for (int q = 0; q < h; ++q) f[q] += f[q + h];
-              sum = f[0];
             }
           }
           __syncwarp();
-          if (have) {
-            uint32_t o[NPAIR];
 #pragma unroll
-            for (int r = 0; r < NPAIR; ++r) {
-              const int lo = slot_logical(BITS, INTER, b_slot(BITS, r, 0));
-              const int hi = slot_logical(BITS, INTER, b_slot(BITS, r, 1));
-              o[r] = prmt(v[lo >> 1], v[hi >> 1],
-                          ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
-            }
-            const int q = wi & (SW - 1);
-            const int cc = q / WPL;
-            const int j = q - cc * WPL;
-            constexpr int PB = WB < XU::U ? WB : XU::U;
-            uint8_t* sbase = row + (wi / SW) * STEP_XB + cc * XU::U;
+          for (int uu = 0; uu < kU; ++uu) {
+            const int wi = w0 + uu * kCT + lane;
+            if (wi < wpr) {
+              uint32_t o[NPAIR];
 #pragma unroll
-            for (int pc = 0; pc < WB / PB; ++pc) {
-              const int lb = j * WB + pc * PB;
-              sts<PB>(sbase + (lb / XU::U) * 4 * XU::U + (lb % XU::U), o + pc * (PB / 4));
+              for (int r = 0; r < NPAIR; ++r) {
+                const int lo = slot_logical(BITS, INTER, b_slot(BITS, r, 0));
+                const int hi = slot_logical(BITS, INTER, b_slot(BITS, r, 1));
+                o[r] = prmt(v[uu][lo >> 1], v[uu][hi >> 1],
+                            ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
+              }
+              const int q = wi & (SW - 1);
+              const int cc = q / WPL;
+              const int j = q - cc * WPL;
+              constexpr int PB = WB < XU::U ? WB : XU::U;
+              uint8_t* sbase = row + (wi / SW) * STEP_XB + cc * XU::U;
+#pragma unroll
+              for (int pc = 0; pc < WB / PB; ++pc) {
+                const int lb = j * WB + pc * PB;
+                sts<PB>(sbase + (lb / XU::U) * 4 * XU::U + (lb % XU::U), o + pc * (PB / 4));
+              }
             }
           }
           if constexpr (!SYM) {
-            // Steps are SW consecutive words (w0 is a multiple of 32).
 #pragma unroll
             for (int off = SW / 2; off >= 1; off >>= 1)
-              sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            if ((lane & (SW - 1)) == 0 && have) sstep[m * spr + wi / SW] = sum;
+#pragma unroll
+              for (int uu = 0; uu < kU; ++uu)
+                sum[uu] += __shfl_xor_sync(0xffffffffu, sum[uu], off);
+#pragma unroll
+            for (int uu = 0; uu < kU; ++uu) {
+              const int wi = w0 + uu * kCT + lane;
+              if ((lane & (SW - 1)) == 0 && wi < wpr) sstep[m * spr + wi / SW] = sum[uu];
+            }
           }
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pro_bar[0]);
-    if (!warp_wait(&pro_bar[0], 0)) return;
+    named_sync(1, kStreamNCW * 32);
     // Prologue 2: the activation sum of every group (per-channel: of the
     // whole row); symmetric formats need none.
     if constexpr (SYM) {
+    } else if (!x_ok_wait) {
     } else if constexpr (GROUPED) {
       const int spg = p.gsize / SC;
       for (int e = tid; e < p.M * p.G; e += kCT) {
@@ -479,9 +493,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         if (lane == 0) sxg[cw] = sum;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pro_bar[1]);
-    if (!warp_wait(&pro_bar[1], 0)) return;
+    named_sync(1, kStreamNCW * 32);
+    if (tid == 0) mbar_arrive(sx_ready);
+    if (!x_ok_wait) return;
 
     // Main loop. Work units (grouped: gslots consecutive groups; per-channel:
     // one step) go to warps round-robin by their index over the whole CTA.
