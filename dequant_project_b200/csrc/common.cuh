@@ -101,6 +101,71 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok);
 }
 
+// ---- thread-block clusters (distributed shared memory) ----
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of all CTAs of the cluster; used once after barrier init so that
+// no CTA touches a peer's barriers before they exist. (Hardware barrier: the
+// CTAs of a cluster are always co-scheduled.)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// Address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+  return d;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (address from
+// map_to_rank), releasing this thread's earlier writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_addr)
+               : "memory");
+}
+
+// Bounded wait, acquiring at cluster scope (for barriers that peers arrive on).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity) {
+  bool ok = mbar_try_wait_cluster(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+      if (mbar_try_wait_cluster(bar, parity)) {
+        ok = true;
+        break;
+      }
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        atomicOr(&g_status, kStatusWaitTimeout);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Untiled bulk copy global -> this CTA's shared memory, completing as
 // transaction bytes on `bar`. dst, src and bytes must be multiples of 16.
 // No multicast: the source is always this GPU's own memory.

@@ -79,7 +79,8 @@ cudaError_t launch_gemv(const GemvArgs& args, const GemvPlan& plan, cudaStream_t
 constexpr int kStreamNCW = 8;     // consumer (tensor-core) warps
 constexpr int kStreamThreads = 32 * (2 + kStreamNCW);  // + producer + reducer
 constexpr int kStreamNRB = 4;     // tile reduction buffers
-constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations
+constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations (per CTA)
+constexpr int kStreamMaxCluster = 8;          // largest split-K cluster (portable size)
 constexpr int kStreamStageBytes = 64 * 1024;   // target packed bytes per stage (long row runs)
 constexpr int kStreamMaxFixedBytes = 128 * 1024;  // cap on everything but the ring
 constexpr int kStreamMaxMeta = 8;  // tile metadata buffers
@@ -94,16 +95,17 @@ struct StreamParams {
   int M, N, K, G, gsize;
   int mp;                 // columns per group slot of the MMA's N=8 side (1,2,4,8)
   int KS, n_slabs, stages, n_meta;
+  int C, KC;              // cluster size (split K) and codes per CTA's K slice
   int w_pitch, xp;        // bytes per packed row in a stage; per activation row
   int stage_bytes;
-  int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar;
+  int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar, off_xred;
   long long tail_first;   // first scales/zeros element past the last 16-byte boundary
   int tail_n;             // number of such elements (0..7)
 };
 
 struct StreamPlan {
-  int wpl, mp, ks, n_slabs, stages, n_meta, w_pitch, xp, stage_bytes;
-  int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar;
+  int wpl, mp, ks, n_slabs, stages, n_meta, w_pitch, xp, stage_bytes, C, KC;
+  int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar, off_xred;
   int smem, grid;
 };
 

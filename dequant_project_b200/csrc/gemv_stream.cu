@@ -39,18 +39,31 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   StreamPlan pl;
   pl.wpl = wpl;
   pl.mp = mp;
+  // Split K over a cluster of C CTAs when the activations do not fit one
+  // CTA: each keeps a slice of KC codes (whole consumer units) resident.
   // Activation rows: 32 bytes of padding past a 128-byte multiple, so that the
   // eight rows an M=8 B-fragment load touches fall on distinct bank groups.
-  pl.xp = round_up(K * 2, 128) + 32;
+  int C = 1, KC = K;
+  for (;;) {
+    KC = round_up((K + C - 1) / C, uc);
+    if ((C - 1) * KC < K && M * (round_up(KC * 2, 128) + 32) <= kStreamXMaxBytes) break;
+    C *= 2;
+    if (C > kStreamMaxCluster || C > num_sms) return false;
+  }
+  pl.C = C;
+  pl.KC = KC;
+  pl.xp = round_up(KC * 2, 128) + 32;
   const int x_bytes = round_up(M * pl.xp, 128);
-  if (x_bytes > kStreamXMaxBytes) return false;
+  const int Gs = grouped ? KC / group_size : 1;
   int off = 0;
   pl.off_x = off;
   off += x_bytes;
   pl.off_sstep = off;
-  off += round_up(M * (K / sc) * 4, 128);
+  off += round_up(M * (KC / sc) * 4, 128);
   pl.off_sx = off;
-  off += round_up(M * G * 4, 128);
+  off += round_up(M * Gs * 4, 128);
+  pl.off_xred = off;  // rank 0's slots for the peers' tile partials
+  if (C > 1) off += round_up(kStreamNRB * C * kTile * M * 4, 128);
   // Metadata: a ring of tile buffers, each [scales span | zeros span] of 16
   // rows x G fp16 plus up to 16 bytes of alignment slack.
   pl.meta_half = round_up(kTile * G * 2 + 32, 128);
@@ -63,12 +76,12 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   if (off + 2 * pl.meta_stride > kStreamMaxFixedBytes) return false;
   // Slabs: about kStreamStageBytes of packed weights per 16-row stage, in
   // whole consumer units.
-  const int64_t row_bytes = static_cast<int64_t>(K) * bits / 8;
-  int n_slabs = static_cast<int>((kTile * row_bytes + kStreamStageBytes - 1) / kStreamStageBytes);
+  const int64_t slice_bytes = static_cast<int64_t>(KC) * bits / 8;
+  int n_slabs = static_cast<int>((kTile * slice_bytes + kStreamStageBytes - 1) / kStreamStageBytes);
   if (n_slabs < 1) n_slabs = 1;
-  int ks = round_up((K + n_slabs - 1) / n_slabs, uc);
-  if (ks > K) ks = K;
-  n_slabs = (K + ks - 1) / ks;
+  int ks = round_up((KC + n_slabs - 1) / n_slabs, uc);
+  if (ks > KC) ks = KC;
+  n_slabs = (KC + ks - 1) / ks;
   pl.ks = ks;
   pl.n_slabs = n_slabs;
   pl.w_pitch = round_up(ks * bits / 8, 128) + 16 * wpl;
@@ -94,9 +107,13 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   pl.off_meta += ring;
   pl.off_red += ring;
   pl.off_bar += ring;
+  pl.off_xred += ring;
   pl.smem = ring + off;
+  // Clusters (each a set of C CTAs on C SMs sharing rows); the launch caps
+  // them at the number that can be resident at once.
   const int tiles = (N + kTile - 1) / kTile;
-  pl.grid = tiles < num_sms ? tiles : num_sms;
+  const int clusters = num_sms / C;
+  pl.grid = C * (tiles < clusters ? tiles : clusters);
   *plan = pl;
   return true;
 }
@@ -129,6 +146,9 @@ cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t 
   p.meta_stride = pl.meta_stride;
   p.off_red = pl.off_red;
   p.off_bar = pl.off_bar;
+  p.off_xred = pl.off_xred;
+  p.C = pl.C;
+  p.KC = pl.KC;
   const long long total = static_cast<long long>(a.N) * p.G;
   p.tail_first = total / 8 * 8;
   p.tail_n = static_cast<int>(total - p.tail_first);

@@ -222,16 +222,28 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint64_t* red_empty = red_full + kStreamNRB;  // [kStreamNRB]
   uint64_t* x_full = red_empty + kStreamNRB;
   uint64_t* sx_ready = x_full + 1;              // activation sums written (reducer)
+  uint64_t* xfull = sx_ready + 1;               // [kStreamNRB] peers' partials landed (rank 0)
+  uint64_t* xempty = xfull + kStreamNRB;        // [kStreamNRB] rank 0 done with a slot (rank > 0)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.stages;
   const int NMB = p.n_meta;
+  // Split K: a cluster of C CTAs shares the same rows; CTA `rank` streams the
+  // K slice [klo, klo + kn) with those activations resident, and rank 0 sums
+  // the C partials of every tile through distributed shared memory.
+  const int C = p.C;
+  const int rank = C > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int cid = static_cast<int>(blockIdx.x) / C;
+  const int ncl = static_cast<int>(gridDim.x) / C;
+  const int klo = rank * p.KC;
+  const int kn = min(p.KC, p.K - klo);
+  const int n_slabs = (kn + p.KS - 1) / p.KS;
   const int64_t row_bytes = static_cast<int64_t>(p.K) * BITS / 8;
-  const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
-  const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
+  const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * cid / ncl);
+  const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (cid + 1) / ncl);
   const int n_tiles = (row_end - row_begin + kTile - 1) / kTile;
-  const int total = n_tiles * p.n_slabs;
+  const int total = n_tiles * n_slabs;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -245,9 +257,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     mbar_init(x_full, 1);
     mbar_init(sx_ready, 1);
+    for (int b = 0; b < kStreamNRB; ++b) {
+      mbar_init(&xfull[b], 32 * (C - 1));
+      mbar_init(&xempty[b], 1);
+    }
     fence_mbar_init();
   }
   __syncthreads();
+  // Peers arrive on each other's barriers: all of them must exist first.
+  if (C > 1) cluster_sync_all();
   if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
@@ -259,7 +277,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // boundary cannot be bulk-copied; the last CTA reads them here and stores
     // them into its final tile's metadata buffer.
     uint16_t tail_s = 0, tail_z = 0;
-    if (blockIdx.x == gridDim.x - 1 && lane < p.tail_n) {
+    if (cid == ncl - 1 && lane < p.tail_n) {
       tail_s = p.scales[p.tail_first + lane];
       if (!SYM) tail_z = p.zeros[p.tail_first + lane];
     }
@@ -295,11 +313,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
     };
     auto issue_stage = [&](int s) {
-      const int i = s / p.n_slabs, j = s - (s / p.n_slabs) * p.n_slabs;
+      const int i = s / n_slabs, j = s - (s / n_slabs) * n_slabs;
       const int r0 = row_begin + i * kTile;
       const int R = min(kTile, row_end - r0);
-      const int k0 = j * p.KS;
-      const int L = min(p.KS, p.K - k0);
+      const int k0 = klo + j * p.KS;
+      const int L = min(p.KS, klo + kn - k0);
       const uint32_t run = static_cast<uint32_t>(L) * BITS / 8;
       const int slot = s % S;
       uint8_t* st = smem + slot * p.stage_bytes;
@@ -317,27 +335,27 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int pre = 0;
     for (int s = 0; s < pre; ++s) issue_stage(s);
     pdl_wait_prior_grid();
-    if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * p.K * 2);
+    if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * kn * 2);
     __syncwarp();
     if (lane < p.M)
-      bulk_g2s(smem + p.off_x + lane * p.xp, p.x + static_cast<int64_t>(lane) * p.K,
-               static_cast<uint32_t>(p.K) * 2, x_full, pol_x);
+      bulk_g2s(smem + p.off_x + lane * p.xp, p.x + static_cast<int64_t>(lane) * p.K + klo,
+               static_cast<uint32_t>(kn) * 2, x_full, pol_x);
     int s = pre;
     for (; s < total; ++s) {
       const int slot = s % S;
       if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) break;
-      const int i = s / p.n_slabs;
-      if (i >= NMB && s == i * p.n_slabs) {
+      const int i = s / n_slabs;
+      if (i >= NMB && s == i * n_slabs) {
         // Metadata buffer i % NMB is free once tile i - NMB is consumed: its
         // last stage t released (implied by the wait above when t <= s - S).
-        const int t = (i - NMB + 1) * p.n_slabs - 1;
+        const int t = (i - NMB + 1) * n_slabs - 1;
         if (t > s - S && !warp_wait(&empty[t % S], (t / S) & 1)) break;
       }
       issue_stage(s);
     }
     // Drain: every copy this warp issued has landed before the CTA exits.
     for (int t = max(0, s - S); t < s; ++t) mbar_wait(&full[t % S], (t / S) & 1);
-    const int issued_tiles = (s + p.n_slabs - 1) / p.n_slabs;
+    const int issued_tiles = (s + n_slabs - 1) / n_slabs;
     for (int ii = max(0, issued_tiles - NMB); ii < issued_tiles; ++ii)
       mbar_wait(&meta_full[ii % NMB], (ii / NMB) & 1);
     mbar_wait(x_full, 0);
@@ -362,23 +380,66 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
       const float* red = reinterpret_cast<const float*>(smem + p.off_red) +
                          b * (kStreamNCW * kTile * p.M);
-      for (int idx0 = 0; idx0 < kTile * p.M; idx0 += 32) {
-        const int idx = idx0 + lane;
+      // This CTA's partial of each (row, activation row) of the tile: up to 4
+      // elements per lane (16 rows x M <= 128).
+      float part[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = q * 32 + lane;
         const int row = idx & (kTile - 1);
         const int m = idx >> 4;
         const float s_row = __shfl_sync(0xffffffffu, sc, row);
         const float z_row = __shfl_sync(0xffffffffu, zc, row);
+        part[q] = 0.f;
         if (idx < kTile * p.M && row < R) {
           float sum = 0.f;
 #pragma unroll
           for (int w = 0; w < kStreamNCW; ++w) sum += red[(w * kTile + row) * p.M + m];
           if constexpr (!GROUPED) sum = s_row * (SYM ? sum : fmaf(-(z_row - kBias), sxg[m], sum));
-          p.y[static_cast<int64_t>(m) * p.N + r0 + row] =
-              __half_as_ushort(__float2half_rn(sum));
+          part[q] = sum;
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_empty[b]);
+      float* xred = reinterpret_cast<float*>(smem + p.off_xred) + b * (C * kTile * p.M);
+      if (C > 1 && rank > 0) {
+        // Send the partial to rank 0's slot b (free once rank 0 released it
+        // for tile i - kStreamNRB), then arrive there.
+        if (i >= kStreamNRB && !warp_wait_cluster(&xempty[b], ((i / kStreamNRB) - 1) & 1))
+          return;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int idx = q * 32 + lane;
+          const int row = idx & (kTile - 1);
+          if (idx < kTile * p.M && row < R)
+            st_cluster_f32(map_to_rank(xred + rank * kTile * p.M + (idx >> 4) * kTile + row, 0),
+                           part[q]);
+        }
+        mbar_arrive_remote(map_to_rank(&xfull[b], 0));
+        continue;
+      }
+      if (C > 1 && !warp_wait_cluster(&xfull[b], (i / kStreamNRB) & 1)) return;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = q * 32 + lane;
+        const int row = idx & (kTile - 1);
+        const int m = idx >> 4;
+        if (idx < kTile * p.M && row < R) {
+          float sum = part[q];
+          for (int r = 1; r < C; ++r) sum += xred[r * kTile * p.M + m * kTile + row];
+          p.y[static_cast<int64_t>(m) * p.N + r0 + row] = __half_as_ushort(__float2half_rn(sum));
+        }
+      }
+      if (C > 1) {
+        __syncwarp();
+        if (lane >= 1 && lane < C) mbar_arrive_remote(map_to_rank(&xempty[b], lane));
+      }
+    }
+    // A peer leaves only once rank 0 has released every slot it used, so no
+    // remote arrive can target a CTA that has exited.
+    if (C > 1 && rank > 0) {
+      for (int i = max(0, n_tiles - kStreamNRB); i < n_tiles; ++i)
+        if (!warp_wait_cluster(&xempty[i % kStreamNRB], (i / kStreamNRB) & 1)) return;
     }
   } else {
     // ----------------------------------------------------------- consumers
@@ -388,7 +449,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     constexpr int kCT = kStreamNCW * 32;
     float* sstep = reinterpret_cast<float*>(smem + p.off_sstep);
     float* sxg = reinterpret_cast<float*>(smem + p.off_sx);
-    const int spr = p.K / SC;  // steps per activation row
+    const int spr = kn / SC;   // steps per activation row (this CTA's K slice)
+    const int Gs = GROUPED ? kn / p.gsize : 1;  // groups in the slice
+    const int g_lo = GROUPED ? klo / p.gsize : 0;
 
     // Prologue 1: activations, in place, into B-fragment order, with per-step
     // sums (asymmetric formats only). One word per lane per chunk of 32; a
@@ -401,7 +464,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const bool x_ok_wait = warp_wait(x_full, 0);
     if (x_ok_wait) {
       constexpr int kU = 4;
-      const int wpr = p.K / PP;
+      const int wpr = kn / PP;
       for (int m = 0; m < p.M; ++m) {
         uint8_t* row = smem + p.off_x + m * p.xp;
         for (int w0 = cw * 32; w0 < wpr; w0 += kU * kCT) {
@@ -476,9 +539,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     } else if (!x_ok_wait) {
     } else if constexpr (GROUPED) {
       const int spg = p.gsize / SC;
-      for (int e = tid; e < p.M * p.G; e += kCT) {
-        const int m = e / p.G;
-        const int g = e - m * p.G;
+      for (int e = tid; e < p.M * Gs; e += kCT) {
+        const int m = e / Gs;
+        const int g = e - m * Gs;
         const float* src = sstep + m * spr + g * spg;
         float sum = 0.f;
         for (int t = 0; t < spg; ++t) sum += src[t];
@@ -509,7 +572,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const uint8_t* xrow_base = smem + p.off_x + (x_ok ? my_xrow : 0) * p.xp + c * XU::U;
     constexpr int kStepWB = SC * BITS / 8;  // packed bytes per step per row
     const int spg = p.gsize / SC;
-    const int units_per_tile = GROUPED ? (p.G + gslots - 1) / gslots : spr;
+    const int units_per_tile = GROUPED ? (Gs + gslots - 1) / gslots : spr;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float D[NSET][NF][4];
 #pragma unroll
@@ -530,11 +593,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       // Byte offsets of (row gid, group 0) and (row gid + 8, group 0).
       const int mo_a = static_cast<int>(static_cast<int64_t>(r0 + gid) * p.G * 2 - a0);
       const int mo_b = mo_a + 8 * p.G * 2;
-      for (int j = 0; j < p.n_slabs; ++j, ++s) {
+      for (int j = 0; j < n_slabs; ++j, ++s) {
         const int slot = s % S;
         if (!warp_wait(&full[slot], (s / S) & 1)) return;
-        const int k0 = j * p.KS;
-        const int L = min(p.KS, p.K - k0);
+        const int k0 = klo + j * p.KS;          // absolute K of the slab
+        const int L = min(p.KS, klo + kn - k0);
+        const int kx0 = k0 - klo;               // its offset in the resident slice
         const uint8_t* st = smem + slot * p.stage_bytes;
         const uint8_t* wa_row = st + gid * p.w_pitch + c * WPL * 4;
         const uint8_t* wb_row = wa_row + 8 * p.w_pitch;
@@ -542,7 +606,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           const int g_slab = k0 / p.gsize;
           const int ng = L / p.gsize;
           const int units = (ng + gslots - 1) / gslots;
-          const int ubase = i * units_per_tile + g_slab / gslots;
+          const int ubase = i * units_per_tile + (g_slab - g_lo) / gslots;
           for (int u = (cw - ubase % kStreamNCW + kStreamNCW) % kStreamNCW; u < units;
                u += kStreamNCW) {
 #pragma unroll
@@ -567,7 +631,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
               sv[e] = __half2float(*reinterpret_cast<const __half*>(meta + mo));
               if constexpr (!SYM) {
                 zv[e] = __half2float(*reinterpret_cast<const __half*>(meta + p.meta_half + mo));
-                sxv[e] = sxg[(ev[e] ? xrow : 0) * p.G + g];
+                sxv[e] = sxg[(ev[e] ? xrow : 0) * Gs + (g - g_lo)];
               } else {
                 zv[e] = 0.f;
                 sxv[e] = 0.f;
@@ -578,7 +642,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
               const int st0 = u * gslots;
               const uint8_t* pwa = wa_row + st0 * kStepWB;
               const uint8_t* pwb = wb_row + st0 * kStepWB;
-              const uint8_t* px = xrow_base + (k0 / SC + st0) * STEP_XB;
+              const uint8_t* px = xrow_base + (kx0 / SC + st0) * STEP_XB;
 #pragma unroll
               for (int gs = 0; gs < gslots; ++gs)
                 mma_step<BITS, WPL, NSET>(pwa + gs * kStepWB, pwb + gs * kStepWB,
@@ -589,7 +653,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                 if (gl >= ng) break;
                 const bool live = x_ok && my_slot == gs;
                 const int st0 = gl * spg;         // first step of the group in the slab
-                const int kst = k0 / SC + st0;    // its step index along K
+                const int kst = kx0 / SC + st0;   // its step index in the slice
                 for (int t = 0; t < spg; ++t) {
                   const int wofs = (st0 + t) * kStepWB;
                   mma_step<BITS, WPL, NSET>(wa_row + wofs, wb_row + wofs,
@@ -610,7 +674,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           }
         } else {
           const int steps = L / SC;
-          const int st_glob0 = k0 / SC;
+          const int st_glob0 = kx0 / SC;
           const int ubase = i * units_per_tile + st_glob0;
           int u = (cw - ubase % kStreamNCW + kStreamNCW) % kStreamNCW;
           // Two steps per iteration: the second one's loads overlap the first
@@ -696,12 +760,30 @@ cudaError_t launch_one(const StreamParams& p, int grid, int smem, cudaStream_t s
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   // Programmatic dependent launch: this grid may start while the previous
-  // one drains; it waits for it before reading activations.
-  cudaLaunchAttribute attr[1];
+  // one drains; it waits for it before reading activations. Split-K runs as
+  // clusters of p.C CTAs.
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.C > 1 ? 2 : 1;
+  if (p.C > 1) {
+    // No more clusters than can be resident at once (the plan assumed every
+    // SM; GPC boundaries can leave some out). Cached per device and size.
+    static int cached_n[64][kStreamMaxCluster + 1] = {};
+    int n = (dev >= 0 && dev < 64) ? cached_n[dev][p.C] : 0;
+    if (n == 0) {
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return e;
+      if (n < 1) return cudaErrorInvalidConfiguration;
+      if (dev >= 0 && dev < 64) cached_n[dev][p.C] = n;
+    }
+    if (grid / p.C > n) cfg.gridDim = dim3(n * p.C);
+  }
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 

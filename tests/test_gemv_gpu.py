@@ -117,6 +117,29 @@ def test_ragged_shapes(n, k, bits, gs):
 BENCH = [(8, None, True), (4, 128, False), (2, 64, False)]
 
 
+# Activations too large for one CTA's shared memory (M x K x 2 > 100 KB) are
+# split along K over a cluster of 2, 4 or 8 CTAs that combine their partial
+# sums through distributed shared memory.
+SPLIT_K = [
+    (1000, 11008, 4, 128, False, 8),   # 2 CTAs per cluster
+    (333, 11008, 2, 64, False, 8),
+    (517, 11008, 8, None, True, 8),    # per-channel
+    (257, 11008, 8, None, False, 6),   # per-channel, asymmetric
+    (1000, 12288, 4, 128, True, 5),
+    (300, 16384, 4, 64, False, 8),     # 4 CTAs
+    (200, 28672, 4, 128, False, 8),    # 8 CTAs
+    (129, 28672, 2, 64, True, 7),
+    (64, 24576, 8, 128, False, 8),
+]
+
+
+@pytest.mark.parametrize("n,k,bits,gs,sym,m", SPLIT_K,
+                         ids=lambda v: str(v))
+def test_split_k_clusters(n, k, bits, gs, sym, m):
+    run_case(n, k, bits, gs, sym, "sequential", m, seed=n + k + m)
+    run_case(n, k, bits, gs, sym, "interleaved", m, seed=n + k + m + 1)
+
+
 @pytest.mark.parametrize("m", (1, 4, 8))
 @pytest.mark.parametrize("n,k", [(4096, 11008), (11008, 4096)])
 @pytest.mark.parametrize("fmt", BENCH, ids=("int8-perch-sym", "int4-g128-asym", "int2-g64-asym"))
