@@ -82,7 +82,6 @@ constexpr int kStreamNRB = 4;     // tile reduction buffers
 constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations (per CTA)
 constexpr int kStreamMaxCluster = 8;          // largest split-K cluster (portable size)
 constexpr int kStreamStageBytes = 64 * 1024;   // target packed bytes per stage (long row runs)
-constexpr int kStreamMaxFixedBytes = 128 * 1024;  // cap on everything but the ring
 constexpr int kStreamMaxMeta = 8;  // tile metadata buffers
 constexpr int kStreamBarBytes = 512;
 

@@ -43,10 +43,31 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   // CTA: each keeps a slice of KC codes (whole consumer units) resident.
   // Activation rows: 32 bytes of padding past a 128-byte multiple, so that the
   // eight rows an M=8 B-fragment load touches fall on distinct bank groups.
+  // The smallest C whose slice's activations, sums, metadata ring (two
+  // buffers), reduction buffers and two 16-row stages fit.
+  const int meta_stride = 2 * round_up(kTile * G * 2 + 32, 128);
+  // Bytes of one 16-row stage when a slice of kc codes is cut into slabs of
+  // about kStreamStageBytes (whole units).
+  auto slab_codes = [&](int kc) {
+    const int64_t bytes = static_cast<int64_t>(kc) * bits / 8;
+    int ns = static_cast<int>((kTile * bytes + kStreamStageBytes - 1) / kStreamStageBytes);
+    if (ns < 1) ns = 1;
+    int ks = round_up((kc + ns - 1) / ns, uc);
+    return ks > kc ? kc : ks;
+  };
+  auto stage_bytes_for = [&](int kc) {
+    return round_up(kTile * (round_up(slab_codes(kc) * bits / 8, 128) + 16 * wpl), 128);
+  };
+  const int red_bytes = round_up(kStreamNRB * kStreamNCW * kTile * M * 4, 128);
   int C = 1, KC = K;
   for (;;) {
     KC = round_up((K + C - 1) / C, uc);
-    if ((C - 1) * KC < K && M * (round_up(KC * 2, 128) + 32) <= kStreamXMaxBytes) break;
+    const int xb = round_up(M * (round_up(KC * 2, 128) + 32), 128);
+    const int need = xb + round_up(M * (KC / sc) * 4, 128) +
+                     round_up(M * (grouped ? KC / group_size : 1) * 4, 128) +
+                     (C > 1 ? round_up(kStreamNRB * C * kTile * M * 4, 128) : 0) + red_bytes +
+                     kStreamBarBytes + 2 * meta_stride + 2 * stage_bytes_for(KC);
+    if ((C - 1) * KC < K && xb <= kStreamXMaxBytes && need <= kMaxSmemBytes) break;
     C *= 2;
     if (C > kStreamMaxCluster || C > num_sms) return false;
   }
@@ -73,15 +94,10 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   pl.off_bar = off;
   off += kStreamBarBytes;
   pl.off_meta = off;  // NMB tile metadata buffers follow
-  if (off + 2 * pl.meta_stride > kStreamMaxFixedBytes) return false;
   // Slabs: about kStreamStageBytes of packed weights per 16-row stage, in
   // whole consumer units.
-  const int64_t slice_bytes = static_cast<int64_t>(KC) * bits / 8;
-  int n_slabs = static_cast<int>((kTile * slice_bytes + kStreamStageBytes - 1) / kStreamStageBytes);
-  if (n_slabs < 1) n_slabs = 1;
-  int ks = round_up((KC + n_slabs - 1) / n_slabs, uc);
-  if (ks > KC) ks = KC;
-  n_slabs = (KC + ks - 1) / ks;
+  const int ks = slab_codes(KC);
+  const int n_slabs = (KC + ks - 1) / ks;
   pl.ks = ks;
   pl.n_slabs = n_slabs;
   pl.w_pitch = round_up(ks * bits / 8, 128) + 16 * wpl;
