@@ -28,10 +28,10 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   const int sc = 4 * wpl * pp;
   const int G = K / group_size;
   const bool grouped = G > 1;
-  // Activation-row columns per group slot: M rounded up to a power of two,
-  // at least 2 (units of at most 4 groups keep every consumer warp busy on
-  // a 40 KB stage); per-channel: all 8 columns are activation rows.
-  int mp = 2;
+  // Activation-row columns per group slot: M rounded up to a power of two
+  // (M = 1: eight groups per unit); per-channel: all 8 columns are
+  // activation rows.
+  int mp = 1;
   while (mp < M) mp <<= 1;
   if (!grouped) mp = 8;
   const int gslots = 8 / mp;

@@ -794,6 +794,7 @@ cudaError_t launch_gs(int gs, const StreamParams& p, int grid, int smem, cudaStr
     case 1: return launch_one<BITS, SYM, INTER, WPL, 1>(p, grid, smem, stream);
     case 2: return launch_one<BITS, SYM, INTER, WPL, 2>(p, grid, smem, stream);
     case 4: return launch_one<BITS, SYM, INTER, WPL, 4>(p, grid, smem, stream);
+    case 8: return launch_one<BITS, SYM, INTER, WPL, 8>(p, grid, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
