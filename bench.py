@@ -243,7 +243,7 @@ def run_ours(args, rank, world, local_rank):
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(per_gpu / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy)",
-                         "kernel": "dqg::gemv_kernel (all 18 launches of a step)",
+                         "kernel": "dqg::stream::gemv_stream_kernel (all 18 launches of a step)",
                          "bytes_per_launch_avg": step_bytes // len(cs),
                          "traffic": traffic},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
