@@ -98,6 +98,7 @@ struct StreamParams {
   int w_pitch, xp;        // bytes per packed row in a stage; per activation row
   int stage_bytes;
   int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar, off_xred;
+  int off_zero;           // zero block for non-live fragment columns
   long long tail_first;   // first scales/zeros element past the last 16-byte boundary
   int tail_n;             // number of such elements (0..7)
 };
@@ -105,6 +106,7 @@ struct StreamParams {
 struct StreamPlan {
   int wpl, mp, ks, n_slabs, stages, n_meta, w_pitch, xp, stage_bytes, C, KC;
   int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar, off_xred;
+  int off_zero;
   int smem, grid;
 };
 

@@ -66,7 +66,7 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
     const int need = xb + round_up(M * (KC / sc) * 4, 128) +
                      round_up(M * (grouped ? KC / group_size : 1) * 4, 128) +
                      (C > 1 ? round_up(kStreamNRB * C * kTile * M * 4, 128) : 0) + red_bytes +
-                     kStreamBarBytes + 2 * meta_stride + 2 * stage_bytes_for(KC);
+                     kStreamBarBytes + 640 + 2 * meta_stride + 2 * stage_bytes_for(KC);
     if ((C - 1) * KC < K && xb <= kStreamXMaxBytes && need <= kMaxSmemBytes) break;
     C *= 2;
     if (C > kStreamMaxCluster || C > num_sms) return false;
@@ -83,6 +83,10 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   off += round_up(M * (KC / sc) * 4, 128);
   pl.off_sx = off;
   off += round_up(M * Gs * 4, 128);
+  // Zero block (one step of activations, 512 bytes at most) whose bank phase
+  // is 64 bytes off the activation rows' (which start at 128-byte multiples).
+  pl.off_zero = off + 64;
+  off += 640;
   pl.off_xred = off;  // rank 0's slots for the peers' tile partials
   if (C > 1) off += round_up(kStreamNRB * C * kTile * M * 4, 128);
   // Metadata: a ring of tile buffers, each [scales span | zeros span] of 16
@@ -124,6 +128,7 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   pl.off_red += ring;
   pl.off_bar += ring;
   pl.off_xred += ring;
+  pl.off_zero += ring;
   pl.smem = ring + off;
   // Clusters (each a set of C CTAs on C SMs sharing rows); the launch caps
   // them at the number that can be resident at once.
@@ -163,6 +168,7 @@ cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t 
   p.off_red = pl.off_red;
   p.off_bar = pl.off_bar;
   p.off_xred = pl.off_xred;
+  p.off_zero = pl.off_zero;
   p.C = pl.C;
   p.KC = pl.KC;
   const long long total = static_cast<long long>(a.N) * p.G;

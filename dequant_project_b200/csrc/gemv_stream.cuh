@@ -146,11 +146,12 @@ struct XUnits {
 };
 
 // One step of one lane: WPL words of rows gid and gid + 8 and their
-// activations (loaded only when this lane's fragment column is live; zero
-// otherwise), NF MMAs per word into chain set j % NSET.
+// activations (px points at the step's activations when this lane's fragment
+// column is live, else at a zero block), NF MMAs per word into chain set
+// j % NSET.
 template <int BITS, int WPL, int NSET>
 __device__ __forceinline__ void mma_step(const uint8_t* pa, const uint8_t* pb, const uint8_t* px,
-                                         bool live, float (&D)[NSET][(16 / BITS) / 2][4]) {
+                                         float (&D)[NSET][(16 / BITS) / 2][4]) {
   constexpr int NPAIR = 16 / BITS;
   constexpr int NF = NPAIR / 2;
   using XU = XUnits<BITS, WPL>;
@@ -158,13 +159,8 @@ __device__ __forceinline__ void mma_step(const uint8_t* pa, const uint8_t* pb, c
   lds<WPL * 4>(pa, wa);
   lds<WPL * 4>(pb, wb);
   uint32_t bx[WPL * NPAIR];
-  if (live) {
 #pragma unroll
-    for (int u = 0; u < XU::NU; ++u) lds<XU::U>(px + u * 4 * XU::U, bx + u * (XU::U / 4));
-  } else {
-#pragma unroll
-    for (int r = 0; r < WPL * NPAIR; ++r) bx[r] = 0u;
-  }
+  for (int u = 0; u < XU::NU; ++u) lds<XU::U>(px + u * 4 * XU::U, bx + u * (XU::U / 4));
 #pragma unroll
   for (int j = 0; j < WPL; ++j) {
     uint32_t ua[NPAIR], ub[NPAIR];
@@ -461,6 +457,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // The consumer warps synchronise the prologue with a named barrier (id 1):
     // every consumer warp reaches both barriers, also when its activation
     // wait gave up, so that none is left waiting; such a warp returns after.
+    for (int i = tid; i < STEP_XB / 16; i += kCT)
+      reinterpret_cast<uint4*>(smem + p.off_zero)[i] = make_uint4(0u, 0u, 0u, 0u);
     const bool x_ok_wait = warp_wait(x_full, 0);
     if (x_ok_wait) {
       constexpr int kU = 4;
@@ -570,6 +568,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int my_xrow = gid - my_slot * mp;
     const bool x_ok = my_xrow < p.M;
     const uint8_t* xrow_base = smem + p.off_x + (x_ok ? my_xrow : 0) * p.xp + c * XU::U;
+    // Lanes whose column is not live read zeros from a block 64 bytes off the
+    // activations' bank phase (no bank conflict with the live lanes).
+    const uint8_t* zero_base = smem + p.off_zero + c * XU::U;
     constexpr int kStepWB = SC * BITS / 8;  // packed bytes per step per row
     const int spg = p.gsize / SC;
     const int units_per_tile = GROUPED ? (Gs + gslots - 1) / gslots : spr;
@@ -646,7 +647,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
               for (int gs = 0; gs < gslots; ++gs)
                 mma_step<BITS, WPL, NSET>(pwa + gs * kStepWB, pwb + gs * kStepWB,
-                                          px + gs * STEP_XB, x_ok && my_slot == gs, D);
+                                          (x_ok && my_slot == gs) ? px + gs * STEP_XB : zero_base,
+                                          D);
             } else {
               for (int gs = 0; gs < gslots; ++gs) {
                 const int gl = u * gslots + gs;
@@ -657,7 +659,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                 for (int t = 0; t < spg; ++t) {
                   const int wofs = (st0 + t) * kStepWB;
                   mma_step<BITS, WPL, NSET>(wa_row + wofs, wb_row + wofs,
-                                            xrow_base + (kst + t) * STEP_XB, live, D);
+                                            live ? xrow_base + (kst + t) * STEP_XB : zero_base, D);
                 }
               }
             }
@@ -681,14 +683,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           // one's MMAs.
           for (; u + kStreamNCW < steps; u += 2 * kStreamNCW) {
             mma_step<BITS, WPL, NSET>(wa_row + u * kStepWB, wb_row + u * kStepWB,
-                                      xrow_base + (st_glob0 + u) * STEP_XB, x_ok, D);
+                                      x_ok ? xrow_base + (st_glob0 + u) * STEP_XB : zero_base, D);
             const int u2 = u + kStreamNCW;
             mma_step<BITS, WPL, NSET>(wa_row + u2 * kStepWB, wb_row + u2 * kStepWB,
-                                      xrow_base + (st_glob0 + u2) * STEP_XB, x_ok, D);
+                                      x_ok ? xrow_base + (st_glob0 + u2) * STEP_XB : zero_base, D);
           }
           if (u < steps)
             mma_step<BITS, WPL, NSET>(wa_row + u * kStepWB, wb_row + u * kStepWB,
-                                      xrow_base + (st_glob0 + u) * STEP_XB, x_ok, D);
+                                      x_ok ? xrow_base + (st_glob0 + u) * STEP_XB : zero_base, D);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
