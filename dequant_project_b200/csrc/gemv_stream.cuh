@@ -21,12 +21,9 @@
 //
 // Exact unpack with compile-time constants: a code pair at bit position p of
 // the two 16-bit halves (p + bits <= 10) is dropped into the mantissa of fp16
-// 1024 by one LOP3 and centred by one HADD2 with -(1024 + c * 2^p), c =
-// 2^(bits - 1), giving (q - c) * 2^p exactly. A word yields its pairs at 1
-// (INT8), 2 (INT4) or 4 (INT2) positions p; each position accumulates in its
-// own MMA chain and the chains are combined in fp32 with exact power-of-two
-// factors. Centring keeps the tensor-core partial sums as small as in a
-// dequantized product. The offset is applied per group in fp32 through the
+// 1024 by one LOP3 and brought to (q - c), c = 2^(bits - 1), by one HADD2
+// (p = 0) or one HFMA2 with the exact scale 2^-p (p > 0). Centring keeps the
+// tensor-core partial sums as small as in a dequantized product. The offset is applied per group in fp32 through the
 // group's activation sum:
 //   sum_k (q - z) x = P - (z - c) * Sx,   P = sum_k (q - c) x,   Sx = sum_k x,
 // so any zero-point (fractional, out of range) is handled the same way, and the
@@ -59,31 +56,36 @@ __host__ __device__ constexpr int b_slot(int bits, int r, int hi) {
   return r + (hi ? 2 : 0);
 }
 
-// Bit position (within a 16-bit half) of the codes of MMA chain mi.
-__host__ __device__ constexpr int chain_pos(int bits, int mi) {
-  return bits == 4 ? 4 * mi : bits == 2 ? 2 * mi : 0;
-}
-
-// Code pairs of one word as centred fp16 integers (q - c) * 2^p, c =
-// 2^(bits - 1), in b_slot order: one LOP3 drops a pair into the mantissa of
-// 1024 (giving 1024 + q * 2^p exactly, p + bits <= 10) and one HADD2 with the
-// constant -(1024 + c * 2^p) leaves (q - c) * 2^p, exactly.
+// Code pairs of one word as centred fp16 integers (q - c), c = 2^(bits - 1),
+// in b_slot order: one LOP3 drops a pair at bit position p into the mantissa
+// of 1024 (1024 + q * 2^p, exactly, p + bits <= 10) and one HADD2 (p = 0) or
+// HFMA2 with 2^-p and -(1024 * 2^-p + c) (p > 0) leaves q - c, exactly (every
+// intermediate is an integer or a power-of-two multiple below 2^11).
 template <int BITS>
 __device__ __forceinline__ void unpack_centered(uint32_t w, uint32_t* pa) {
   constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
   if constexpr (BITS == 4) {
     const uint32_t w8 = prmt(w, 0u, 0x4341u);  // (w >> 8) & 0x00FF00FF
-    pa[0] = hadd2_u32(lop3_and_or(w, 0x000F000Fu, kMagic), 0xE408E408u);   // slots 0, 4 (p = 0)
-    pa[1] = hadd2_u32(lop3_and_or(w8, 0x000F000Fu, kMagic), 0xE408E408u);  // slots 2, 6 (p = 0)
-    pa[2] = hadd2_u32(lop3_and_or(w, 0x00F000F0u, kMagic), 0xE480E480u);   // slots 1, 5 (p = 4)
-    pa[3] = hadd2_u32(lop3_and_or(w8, 0x00F000F0u, kMagic), 0xE480E480u);  // slots 3, 7 (p = 4)
+    pa[0] = hadd2_u32(lop3_and_or(w, 0x000F000Fu, kMagic), 0xE408E408u);   // slots 0, 4: -1032
+    pa[1] = hadd2_u32(lop3_and_or(w8, 0x000F000Fu, kMagic), 0xE408E408u);  // slots 2, 6
+    pa[2] = hfma2_u32(lop3_and_or(w, 0x00F000F0u, kMagic), 0x2C002C00u,
+                      0xD480D480u);                                         // slots 1, 5: /16 - 72
+    pa[3] = hfma2_u32(lop3_and_or(w8, 0x00F000F0u, kMagic), 0x2C002C00u,
+                      0xD480D480u);                                         // slots 3, 7
   } else if constexpr (BITS == 2) {
     const uint32_t w8 = prmt(w, 0u, 0x4341u);
-    constexpr uint32_t kc[4] = {0xE402E402u, 0xE408E408u, 0xE420E420u, 0xE480E480u};
+    // p = 2f: 2^-2f and -(1024 * 2^-2f + 2).
+    constexpr uint32_t kS[4] = {0x3C003C00u, 0x34003400u, 0x2C002C00u, 0x24002400u};
+    constexpr uint32_t kB[4] = {0xE402E402u, 0xDC08DC08u, 0xD420D420u, 0xCC80CC80u};
 #pragma unroll
     for (int f = 0; f < 4; ++f) {
-      pa[2 * f] = hadd2_u32(lop3_and_or(w, 0x00030003u << (2 * f), kMagic), kc[f]);   // f, f + 8
-      pa[2 * f + 1] = hadd2_u32(lop3_and_or(w8, 0x00030003u << (2 * f), kMagic), kc[f]);  // f + 4, f + 12
+      if (f == 0) {
+        pa[0] = hadd2_u32(lop3_and_or(w, 0x00030003u, kMagic), kB[0]);   // slots 0, 8
+        pa[1] = hadd2_u32(lop3_and_or(w8, 0x00030003u, kMagic), kB[0]);  // slots 4, 12
+      } else {
+        pa[2 * f] = hfma2_u32(lop3_and_or(w, 0x00030003u << (2 * f), kMagic), kS[f], kB[f]);
+        pa[2 * f + 1] = hfma2_u32(lop3_and_or(w8, 0x00030003u << (2 * f), kMagic), kS[f], kB[f]);
+      }
     }
   } else {
     pa[0] = hadd2_u32(prmt(w, kMagic, 0x7250u), 0xE480E480u);  // slots 0, 2
@@ -100,6 +102,15 @@ __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uin
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The same MMA with a zero accumulator input (the first MMA of a chain).
+__device__ __forceinline__ void mma16816_first(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
 template <int NB>
@@ -145,15 +156,21 @@ struct XUnits {
   static constexpr int NU = LXB / U;
 };
 
+// Accumulator chains per lane: MMA t of a step goes to chain t % NCH (two
+// independent chains hide the MMA latency).
+template <int BITS, int WPL>
+constexpr int kChains = (WPL * (16 / BITS) / 2) >= 2 ? 2 : 1;
+
 // One step of one lane: WPL words of rows gid and gid + 8 and their
 // activations (px points at the step's activations when this lane's fragment
-// column is live, else at a zero block), NF MMAs per word into chain set
-// j % NSET.
-template <int BITS, int WPL, int NSET>
+// column is live, else at a zero block), NPAIR/2 MMAs per word. FIRST: the
+// chains start here (their first MMA takes a zero accumulator).
+template <int BITS, int WPL, bool FIRST>
 __device__ __forceinline__ void mma_step(const uint8_t* pa, const uint8_t* pb, const uint8_t* px,
-                                         float (&D)[NSET][(16 / BITS) / 2][4]) {
+                                         float (&D)[kChains<BITS, WPL>][4]) {
   constexpr int NPAIR = 16 / BITS;
   constexpr int NF = NPAIR / 2;
+  constexpr int NCH = kChains<BITS, WPL>;
   using XU = XUnits<BITS, WPL>;
   uint32_t wa[WPL], wb[WPL];
   lds<WPL * 4>(pa, wa);
@@ -167,34 +184,30 @@ __device__ __forceinline__ void mma_step(const uint8_t* pa, const uint8_t* pb, c
     unpack_centered<BITS>(wa[j], ua);
     unpack_centered<BITS>(wb[j], ub);
 #pragma unroll
-    for (int mi = 0; mi < NF; ++mi)
-      mma16816(D[j % NSET][mi], ua[2 * mi], ub[2 * mi], ua[2 * mi + 1], ub[2 * mi + 1],
-               bx[j * NPAIR + 2 * mi], bx[j * NPAIR + 2 * mi + 1]);
+    for (int mi = 0; mi < NF; ++mi) {
+      const int t = j * NF + mi;
+      if (FIRST && t < NCH)
+        mma16816_first(D[t % NCH], ua[2 * mi], ub[2 * mi], ua[2 * mi + 1], ub[2 * mi + 1],
+                       bx[j * NPAIR + 2 * mi], bx[j * NPAIR + 2 * mi + 1]);
+      else
+        mma16816(D[t % NCH], ua[2 * mi], ub[2 * mi], ua[2 * mi + 1], ub[2 * mi + 1],
+                 bx[j * NPAIR + 2 * mi], bx[j * NPAIR + 2 * mi + 1]);
+    }
   }
 }
 
-// sum_k (q - c) x of each accumulator element: chains combined with their
-// exact power-of-two factors.
-template <int BITS, int NSET>
-__device__ __forceinline__ void combine(float (&D)[NSET][(16 / BITS) / 2][4], float* P) {
-  constexpr int NF = (16 / BITS) / 2;
+// sum_k (q - c) x of each accumulator element: the chains added in order.
+template <int NCH>
+__device__ __forceinline__ void combine(const float (&D)[NCH][4], float* P) {
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    float v = D[0][0][e];
+    float v = D[0][e];
 #pragma unroll
-    for (int set = 1; set < NSET; ++set) v += D[set][0][e];
-#pragma unroll
-    for (int mi = 1; mi < NF; ++mi) {
-      const float f = 1.0f / static_cast<float>(1 << chain_pos(BITS, mi));
-#pragma unroll
-      for (int set = 0; set < NSET; ++set) v = fmaf(D[set][mi][e], f, v);
-    }
+    for (int ch = 1; ch < NCH; ++ch) v += D[ch][e];
     P[e] = v;
   }
 }
 
-// GS > 0: grouped formats, GS groups per consumer unit (the N=8 side holds
-// 8/GS activation rows x GS group slots); GS == 0: per-channel scales.
 template <int BITS, bool SYM, bool INTER, int WPL, int GS>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     gemv_stream_kernel(const __grid_constant__ StreamParams p) {
@@ -202,12 +215,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   constexpr int MP = GROUPED ? 8 / GS : 8;  // activation-row columns per group slot
   constexpr int PP = 32 / BITS;         // codes per word
   constexpr int NPAIR = PP / 2;         // B registers per word
-  constexpr int NF = NPAIR / 2;         // MMA chains per word (code positions)
   constexpr int SC = 4 * WPL * PP;      // codes per step
   constexpr int WB = PP * 2;            // activation bytes per word
   constexpr int STEP_XB = SC * 2;       // activation bytes per step
   constexpr int SW = 4 * WPL;           // words per step
-  constexpr int NSET = WPL >= 2 ? 2 : 1;
+  constexpr int NCH = kChains<BITS, WPL>;  // accumulator chains
   constexpr float kBias = static_cast<float>(1 << (BITS - 1));
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -575,13 +587,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int spg = p.gsize / SC;
     const int units_per_tile = GROUPED ? (Gs + gslots - 1) / gslots : spr;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float D[NSET][NF][4];
+    float D[NCH][4];
 #pragma unroll
-    for (int set = 0; set < NSET; ++set)
+    for (int ch = 0; ch < NCH; ++ch)
 #pragma unroll
-      for (int mi = 0; mi < NF; ++mi)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
+      for (int e = 0; e < 4; ++e) D[ch][e] = 0.f;
 
     int s = 0;
     for (int i = 0; i < n_tiles; ++i) {
@@ -610,12 +620,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           const int ubase = i * units_per_tile + (g_slab - g_lo) / gslots;
           for (int u = (cw - ubase % kStreamNCW + kStreamNCW) % kStreamNCW; u < units;
                u += kStreamNCW) {
-#pragma unroll
-            for (int set = 0; set < NSET; ++set)
-#pragma unroll
-              for (int mi = 0; mi < NF; ++mi)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
             // This unit's scales, zero-points and activation sums, loaded
             // before its MMAs.
             bool ev[4];
@@ -645,11 +649,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
               const uint8_t* pwb = wb_row + st0 * kStepWB;
               const uint8_t* px = xrow_base + (kx0 / SC + st0) * STEP_XB;
 #pragma unroll
-              for (int gs = 0; gs < gslots; ++gs)
-                mma_step<BITS, WPL, NSET>(pwa + gs * kStepWB, pwb + gs * kStepWB,
-                                          (x_ok && my_slot == gs) ? px + gs * STEP_XB : zero_base,
-                                          D);
+              for (int gs = 0; gs < gslots; ++gs) {
+                const uint8_t* pxg = (x_ok && my_slot == gs) ? px + gs * STEP_XB : zero_base;
+                if (gs == 0)  // the unit's first step starts its chains
+                  mma_step<BITS, WPL, true>(pwa, pwb, pxg, D);
+                else
+                  mma_step<BITS, WPL, false>(pwa + gs * kStepWB, pwb + gs * kStepWB, pxg, D);
+              }
             } else {
+#pragma unroll
+              for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) D[ch][e] = 0.f;
               for (int gs = 0; gs < gslots; ++gs) {
                 const int gl = u * gslots + gs;
                 if (gl >= ng) break;
@@ -658,13 +669,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                 const int kst = kx0 / SC + st0;   // its step index in the slice
                 for (int t = 0; t < spg; ++t) {
                   const int wofs = (st0 + t) * kStepWB;
-                  mma_step<BITS, WPL, NSET>(wa_row + wofs, wb_row + wofs,
+                  mma_step<BITS, WPL, false>(wa_row + wofs, wb_row + wofs,
                                             live ? xrow_base + (kst + t) * STEP_XB : zero_base, D);
                 }
               }
             }
             float P[4];
-            combine<BITS, NSET>(D, P);
+            combine<NCH>(D, P);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (ev[e]) {
@@ -682,14 +693,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           // Two steps per iteration: the second one's loads overlap the first
           // one's MMAs.
           for (; u + kStreamNCW < steps; u += 2 * kStreamNCW) {
-            mma_step<BITS, WPL, NSET>(wa_row + u * kStepWB, wb_row + u * kStepWB,
+            mma_step<BITS, WPL, false>(wa_row + u * kStepWB, wb_row + u * kStepWB,
                                       x_ok ? xrow_base + (st_glob0 + u) * STEP_XB : zero_base, D);
             const int u2 = u + kStreamNCW;
-            mma_step<BITS, WPL, NSET>(wa_row + u2 * kStepWB, wb_row + u2 * kStepWB,
+            mma_step<BITS, WPL, false>(wa_row + u2 * kStepWB, wb_row + u2 * kStepWB,
                                       x_ok ? xrow_base + (st_glob0 + u2) * STEP_XB : zero_base, D);
           }
           if (u < steps)
-            mma_step<BITS, WPL, NSET>(wa_row + u * kStepWB, wb_row + u * kStepWB,
+            mma_step<BITS, WPL, false>(wa_row + u * kStepWB, wb_row + u * kStepWB,
                                       x_ok ? xrow_base + (st_glob0 + u) * STEP_XB : zero_base, D);
         }
         __syncwarp();
@@ -698,13 +709,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
       // Tile end: per (row, activation row) partial of this warp.
       if constexpr (!GROUPED) {
-        combine<BITS, NSET>(D, acc);
+        combine<NCH>(D, acc);
 #pragma unroll
-        for (int set = 0; set < NSET; ++set)
+        for (int ch = 0; ch < NCH; ++ch)
 #pragma unroll
-          for (int mi = 0; mi < NF; ++mi)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) D[set][mi][e] = 0.f;
+          for (int e = 0; e < 4; ++e) D[ch][e] = 0.f;
       }
       // Columns sharing an activation row (different group slots) are summed
       // across lanes: slots are the high bits of the column 2c + (e & 1).
