@@ -113,6 +113,27 @@ __device__ __forceinline__ void mma16816_first(float* d, uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
+// Total of the fp16 values in one word's registers summed over the four lanes
+// of a quad (lanes 4g .. 4g + 3), by MMAs against a matrix of ones: the
+// registers are taken as A fragment registers, whose rows g and g + 8 collect
+// the quad's a0/a2 and a1/a3 halves, so d0 + d2 (every column is the same) is
+// the quad's total. The products are exact and the tensor core accumulates in
+// fp32; one MMA replaces eight conversions, seven adds and two shuffle levels
+// per word.
+template <int NREG>
+__device__ __forceinline__ float quad_sum(const uint32_t* v) {
+  constexpr uint32_t kOnes = 0x3C003C00u;
+  float d[4];
+  if constexpr (NREG == 2) {
+    mma16816_first(d, v[0], v[1], 0u, 0u, kOnes, kOnes);
+  } else {
+    mma16816_first(d, v[0], v[1], v[2], v[3], kOnes, kOnes);
+#pragma unroll
+    for (int i = 4; i < NREG; i += 4) mma16816(d, v[i], v[i + 1], v[i + 2], v[i + 3], kOnes, kOnes);
+  }
+  return d[0] + d[2];
+}
+
 template <int NB>
 __device__ __forceinline__ void lds(const uint8_t* p, uint32_t* r) {
   if constexpr (NB == 4) {
@@ -462,83 +483,100 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int g_lo = GROUPED ? klo / p.gsize : 0;
 
     // Prologue 1: activations, in place, into B-fragment order, with per-step
-    // sums (asymmetric formats only). One word per lane per chunk of 32; a
-    // step's SW words are all in one chunk, so every lane has loaded its words
-    // before any lane overwrites them. Four chunks per pass keep four
-    // independent load/convert/shuffle chains in flight.
+    // sums (asymmetric formats only). Each lane takes one word per chunk of
+    // 32, four chunks per pass. Rows and steps start on multiples of SW words
+    // and chunks on multiples of 32, so a step's SW words are all in one chunk
+    // of one warp: every lane has loaded its words before any lane overwrites
+    // them. A step's sum is the sum of its quads' totals (quad_sum).
     // The consumer warps synchronise the prologue with a named barrier (id 1):
     // every consumer warp reaches both barriers, also when its activation
     // wait gave up, so that none is left waiting; such a warp returns after.
     for (int i = tid; i < STEP_XB / 16; i += kCT)
       reinterpret_cast<uint4*>(smem + p.off_zero)[i] = make_uint4(0u, 0u, 0u, 0u);
     const bool x_ok_wait = warp_wait(x_full, 0);
-    if (x_ok_wait) {
-      constexpr int kU = 4;
-      const int wpr = kn / PP;
+    // Word wi of an activation row, permuted in registers and stored at its
+    // place in the row's B-fragment order.
+    auto put = [&](const uint32_t (&w)[NPAIR], uint8_t* row, int wi) {
+      uint32_t o[NPAIR];
+#pragma unroll
+      for (int r = 0; r < NPAIR; ++r) {
+        const int lo = slot_logical(BITS, INTER, b_slot(BITS, r, 0));
+        const int hi = slot_logical(BITS, INTER, b_slot(BITS, r, 1));
+        o[r] = prmt(w[lo >> 1], w[hi >> 1],
+                    ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
+      }
+      const int q = wi & (SW - 1);
+      const int cc = q / WPL;
+      const int j = q - cc * WPL;
+      constexpr int PB = WB < XU::U ? WB : XU::U;
+      uint8_t* sbase = row + (wi / SW) * STEP_XB + cc * XU::U;
+#pragma unroll
+      for (int pc = 0; pc < WB / PB; ++pc) {
+        const int lb = j * WB + pc * PB;
+        sts<PB>(sbase + (lb / XU::U) * 4 * XU::U + (lb % XU::U), o + pc * (PB / 4));
+      }
+    };
+    constexpr int kU = 4;
+    const int wpr = kn / PP;  // words per activation row
+    if (!x_ok_wait) {
+    } else if constexpr (SYM) {
+      // No sums: row by row (measured faster than the flat order below for
+      // the symmetric formats).
       for (int m = 0; m < p.M; ++m) {
         uint8_t* row = smem + p.off_x + m * p.xp;
         for (int w0 = cw * 32; w0 < wpr; w0 += kU * kCT) {
           uint32_t v[kU][NPAIR];
-          float sum[kU];
 #pragma unroll
           for (int uu = 0; uu < kU; ++uu) {
             const int wi = w0 + uu * kCT + lane;
-            sum[uu] = 0.f;
-            if (wi < wpr) {
-              lds<WB>(row + wi * WB, v[uu]);
-              if constexpr (!SYM) {
-                float f[PP];
-#pragma unroll
-                for (int q = 0; q < NPAIR; ++q) {
-                  const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&v[uu][q]));
-                  f[2 * q] = t.x;
-                  f[2 * q + 1] = t.y;
-                }
-#pragma unroll
-                for (int h = PP / 2; h >= 1; h >>= 1)
-#pragma unroll
-                  for (int q = 0; q < h; ++q) f[q] += f[q + h];
-                sum[uu] = f[0];
-              }
-            }
+            if (wi < wpr) lds<WB>(row + wi * WB, v[uu]);
           }
           __syncwarp();
 #pragma unroll
           for (int uu = 0; uu < kU; ++uu) {
             const int wi = w0 + uu * kCT + lane;
-            if (wi < wpr) {
-              uint32_t o[NPAIR];
-#pragma unroll
-              for (int r = 0; r < NPAIR; ++r) {
-                const int lo = slot_logical(BITS, INTER, b_slot(BITS, r, 0));
-                const int hi = slot_logical(BITS, INTER, b_slot(BITS, r, 1));
-                o[r] = prmt(v[uu][lo >> 1], v[uu][hi >> 1],
-                            ((lo & 1) ? 0x32u : 0x10u) | ((hi & 1) ? 0x7600u : 0x5400u));
-              }
-              const int q = wi & (SW - 1);
-              const int cc = q / WPL;
-              const int j = q - cc * WPL;
-              constexpr int PB = WB < XU::U ? WB : XU::U;
-              uint8_t* sbase = row + (wi / SW) * STEP_XB + cc * XU::U;
-#pragma unroll
-              for (int pc = 0; pc < WB / PB; ++pc) {
-                const int lb = j * WB + pc * PB;
-                sts<PB>(sbase + (lb / XU::U) * 4 * XU::U + (lb % XU::U), o + pc * (PB / 4));
-              }
-            }
+            if (wi < wpr) put(v[uu], row, wi);
           }
-          if constexpr (!SYM) {
+        }
+      }
+    } else {
+      // The words of all M rows as one flat index space (fewer, fuller passes
+      // when a row has fewer than 4 x 256 words).
+      const int wtot = p.M * wpr;
+      // ceil(2^32 / wpr): umulhi(f, wmagic) == f / wpr for every f < 2^32 / wpr.
+      const uint32_t wmagic = 0xFFFFFFFFu / static_cast<uint32_t>(wpr) + 1u;
+      for (int w0 = cw * 32; w0 < wtot; w0 += kU * kCT) {
+        uint32_t v[kU][NPAIR];
+        int mrow[kU], wcol[kU];
 #pragma unroll
-            for (int off = SW / 2; off >= 1; off >>= 1)
+        for (int uu = 0; uu < kU; ++uu) {
+          const int wf = w0 + uu * kCT + lane;
+          const int m = static_cast<int>(__umulhi(static_cast<uint32_t>(wf), wmagic));
+          mrow[uu] = m;
+          wcol[uu] = wf - m * wpr;
+          if (wf < wtot) {
+            lds<WB>(smem + p.off_x + m * p.xp + wcol[uu] * WB, v[uu]);
+          } else {
 #pragma unroll
-              for (int uu = 0; uu < kU; ++uu)
-                sum[uu] += __shfl_xor_sync(0xffffffffu, sum[uu], off);
-#pragma unroll
-            for (int uu = 0; uu < kU; ++uu) {
-              const int wi = w0 + uu * kCT + lane;
-              if ((lane & (SW - 1)) == 0 && wi < wpr) sstep[m * spr + wi / SW] = sum[uu];
-            }
+            for (int r = 0; r < NPAIR; ++r) v[uu][r] = 0u;
           }
+        }
+        float sum[kU];
+#pragma unroll
+        for (int uu = 0; uu < kU; ++uu) sum[uu] = quad_sum<NPAIR>(v[uu]);
+        __syncwarp();
+#pragma unroll
+        for (int uu = 0; uu < kU; ++uu) {
+          if (w0 + uu * kCT + lane < wtot) put(v[uu], smem + p.off_x + mrow[uu] * p.xp, wcol[uu]);
+        }
+#pragma unroll
+        for (int off = SW / 2; off >= 4; off >>= 1)
+#pragma unroll
+          for (int uu = 0; uu < kU; ++uu) sum[uu] += __shfl_xor_sync(0xffffffffu, sum[uu], off);
+#pragma unroll
+        for (int uu = 0; uu < kU; ++uu) {
+          if ((lane & (SW - 1)) == 0 && w0 + uu * kCT + lane < wtot)
+            sstep[mrow[uu] * spr + wcol[uu] / SW] = sum[uu];
         }
       }
     }
