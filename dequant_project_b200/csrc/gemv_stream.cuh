@@ -10,8 +10,9 @@
 //   * warp 0 (producer) streams the CTA's rows as (16-row tile, K slab)
 //     stages into a ring of shared-memory slots: one bulk copy
 //     (cp.async.bulk, no multicast) per packed row segment, plus each tile's
-//     scales/zero-points as one contiguous span. Weights and metadata are
-//     issued before the programmatic-dependent-launch wait, activations after.
+//     scales/zero-points as one contiguous span. The activations are copied
+//     first, right after the programmatic-dependent-launch wait (a copy issued
+//     behind weight copies would wait for them), then the weight ring.
 //   * warps 2.. (consumers) first rewrite the resident activations in place
 //     into the tensor-core B-fragment order and take per-step sums; then, per
 //     stage, unpack codes in registers and run mma.m16n8k16 (fp16 x fp16 ->
@@ -23,8 +24,8 @@
 // the two 16-bit halves (p + bits <= 10) is dropped into the mantissa of fp16
 // 1024 by one LOP3 and brought to (q - c), c = 2^(bits - 1), by one HADD2
 // (p = 0) or one HFMA2 with the exact scale 2^-p (p > 0). Centring keeps the
-// tensor-core partial sums as small as in a dequantized product. The offset is applied per group in fp32 through the
-// group's activation sum:
+// tensor-core partial sums as small as in a dequantized product. The offset is
+// applied per group in fp32 through the group's activation sum:
 //   sum_k (q - z) x = P - (z - c) * Sx,   P = sum_k (q - c) x,   Sx = sum_k x,
 // so any zero-point (fractional, out of range) is handled the same way, and the
 // scale multiplies the group's result in fp32 (as the reference kernel does per
@@ -656,28 +657,57 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           const int ng = L / p.gsize;
           const int units = (ng + gslots - 1) / gslots;
           const int ubase = i * units_per_tile + (g_slab - g_lo) / gslots;
+          // M > 4 (one group per unit): two units per iteration overlap one
+          // unit's epilogue with the next one's loads (measured faster there,
+          // slower for the larger units of M <= 4).
+#pragma unroll(MP == 8 ? 2 : 1)
           for (int u = (cw - ubase % kStreamNCW + kStreamNCW) % kStreamNCW; u < units;
                u += kStreamNCW) {
             // This unit's scales, zero-points and activation sums, loaded
             // before its MMAs.
             bool ev[4];
             float sv[4], zv[4], sxv[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int col = 2 * c + (e & 1);
-              const int slot_e = col / mp;
-              const int xrow = col - slot_e * mp;
-              const int gl = u * gslots + slot_e;
-              ev[e] = gl < ng && xrow < p.M;
-              const int g = g_slab + (ev[e] ? gl : 0);
-              const int mo = ((e >> 1) ? mo_b : mo_a) + g * 2;
-              sv[e] = __half2float(*reinterpret_cast<const __half*>(meta + mo));
+            if constexpr (MP >= 2) {
+              // A lane's two columns 2c, 2c + 1 are one group slot (and two
+              // activation rows): one scale/zero per weight row, one sum per
+              // activation row.
+              const int slot = (2 * c) / MP;
+              const int xr0 = 2 * c - slot * MP;
+              const int gl = u * gslots + slot;
+              const bool gok = gl < ng;
+              const int g = g_slab + (gok ? gl : 0);
+              ev[0] = ev[2] = gok && xr0 < p.M;
+              ev[1] = ev[3] = gok && xr0 + 1 < p.M;
+              sv[0] = sv[1] = __half2float(*reinterpret_cast<const __half*>(meta + mo_a + g * 2));
+              sv[2] = sv[3] = __half2float(*reinterpret_cast<const __half*>(meta + mo_b + g * 2));
               if constexpr (!SYM) {
-                zv[e] = __half2float(*reinterpret_cast<const __half*>(meta + p.meta_half + mo));
-                sxv[e] = sxg[(ev[e] ? xrow : 0) * Gs + (g - g_lo)];
+                const uint8_t* zm = meta + p.meta_half + g * 2;
+                zv[0] = zv[1] = __half2float(*reinterpret_cast<const __half*>(zm + mo_a));
+                zv[2] = zv[3] = __half2float(*reinterpret_cast<const __half*>(zm + mo_b));
+                const float* sx = sxg + (g - g_lo);
+                sxv[0] = sxv[2] = sx[(ev[0] ? xr0 : 0) * Gs];
+                sxv[1] = sxv[3] = sx[(ev[1] ? xr0 + 1 : 0) * Gs];
               } else {
-                zv[e] = 0.f;
-                sxv[e] = 0.f;
+                zv[0] = zv[1] = zv[2] = zv[3] = 0.f;
+                sxv[0] = sxv[1] = sxv[2] = sxv[3] = 0.f;
+              }
+            } else {
+              // One activation row: the lane's two columns are two slots.
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int slot_e = 2 * c + (e & 1);
+                const int gl = u * gslots + slot_e;
+                ev[e] = gl < ng && x_ok;
+                const int g = g_slab + (ev[e] ? gl : 0);
+                const int mo = ((e >> 1) ? mo_b : mo_a) + g * 2;
+                sv[e] = __half2float(*reinterpret_cast<const __half*>(meta + mo));
+                if constexpr (!SYM) {
+                  zv[e] = __half2float(*reinterpret_cast<const __half*>(meta + p.meta_half + mo));
+                  sxv[e] = sxg[g - g_lo];
+                } else {
+                  zv[e] = 0.f;
+                  sxv[e] = 0.f;
+                }
               }
             }
             if (spg == 1 && (u + 1) * gslots <= ng) {
