@@ -39,13 +39,19 @@ def lib() -> ctypes.CDLL:
     h.dqg_dequantize.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, vp]
     h.dqg_device_status.restype = i32
     h.dqg_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
+    h.dqg_add_rms_norm.restype = i32
+    h.dqg_add_rms_norm.argtypes = [vp, vp, vp, vp, i64, i64, ctypes.c_float, vp]
+    h.dqg_rope_kv_append.restype = i32
+    h.dqg_rope_kv_append.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
+    h.dqg_silu_mul.restype = i32
+    h.dqg_silu_mul.argtypes = [vp, vp, i64, i64, vp]
     _lib = h
     return _lib
 
 
 # Every symbol the C header declares; tests check the library exports them all.
 EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_dequantize",
-            "dqg_device_status")
+            "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul")
 
 
 def check(rc: int) -> None:

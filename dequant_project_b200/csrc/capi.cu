@@ -235,6 +235,82 @@ int dqg_dequantize(const int32_t* qweight, const void* scales, const void* zeros
   return ok();
 }
 
+int dqg_add_rms_norm(void* h, const void* delta, const void* weight, void* y, int64_t M,
+                     int64_t H, float eps, void* stream) {
+  if (M < 1 || M > 65535) return fail(DQG_ERR_INVALID, "M must be in [1, 65535], got %lld", (long long)M);
+  if (H < 8 || H % 8 != 0 || H > (1 << 24))
+    return fail(DQG_ERR_INVALID, "H must be a positive multiple of 8, got %lld", (long long)H);
+  if (!(eps >= 0.f)) return fail(DQG_ERR_INVALID, "eps must be non-negative");
+  const void* ptrs[4] = {h, delta, weight, y};
+  const char* names[4] = {"h", "delta", "weight", "y"};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  for (int i = 0; i < 4; ++i) {
+    if (i == 1 && delta == nullptr) continue;
+    int rc = check_device_ptr(ptrs[i], dev, names[i]);
+    if (rc) return rc;
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16)
+      return fail(DQG_ERR_INVALID, "%s must be 16-byte aligned", names[i]);
+  }
+  e = dqg::launch_add_rms_norm(h, delta, weight, y, static_cast<int>(M), static_cast<int>(H), eps,
+                               static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add_rms_norm launch");
+  return ok();
+}
+
+int dqg_rope_kv_append(const void* qkv, const float* cos_row, const float* sin_row, void* q_out,
+                       void* k_cache, void* v_cache, int64_t M, int64_t n_q_heads,
+                       int64_t n_kv_heads, int64_t head_dim, int64_t pos, int64_t capacity,
+                       void* stream) {
+  if (M < 1 || M > 65535) return fail(DQG_ERR_INVALID, "M must be in [1, 65535], got %lld", (long long)M);
+  if (n_q_heads < 1 || n_kv_heads < 1 || n_q_heads + n_kv_heads > 65535)
+    return fail(DQG_ERR_INVALID, "head counts out of range (%lld query, %lld KV)",
+                (long long)n_q_heads, (long long)n_kv_heads);
+  if (head_dim < 2 || head_dim % 2 != 0 || head_dim > 1024)
+    return fail(DQG_ERR_INVALID, "head_dim must be even and at most 1024, got %lld",
+                (long long)head_dim);
+  if (capacity < 1 || pos < 0 || pos >= capacity)
+    return fail(DQG_ERR_INVALID, "position %lld outside the cache (capacity %lld)",
+                (long long)pos, (long long)capacity);
+  if (M * n_kv_heads * capacity * head_dim > (int64_t(1) << 40))
+    return fail(DQG_ERR_INVALID, "cache too large");
+  const void* ptrs[6] = {qkv, cos_row, sin_row, q_out, k_cache, v_cache};
+  const char* names[6] = {"qkv", "cos", "sin", "q_out", "k_cache", "v_cache"};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  for (int i = 0; i < 6; ++i) {
+    int rc = check_device_ptr(ptrs[i], dev, names[i]);
+    if (rc) return rc;
+  }
+  e = dqg::launch_rope_kv_append(qkv, cos_row, sin_row, q_out, k_cache, v_cache,
+                                 static_cast<int>(M), static_cast<int>(n_q_heads),
+                                 static_cast<int>(n_kv_heads), static_cast<int>(head_dim),
+                                 static_cast<int>(pos), static_cast<int>(capacity),
+                                 static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_kv_append launch");
+  return ok();
+}
+
+int dqg_silu_mul(const void* gate_up, void* out, int64_t M, int64_t I, void* stream) {
+  if (M < 1 || I < 1 || M * I > (int64_t(1) << 40))
+    return fail(DQG_ERR_INVALID, "M and I must be positive (got %lld, %lld)", (long long)M,
+                (long long)I);
+  if (I > (int64_t(1) << 30)) return fail(DQG_ERR_INVALID, "I too large");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int rc = check_device_ptr(gate_up, dev, "gate_up");
+  if (rc) return rc;
+  rc = check_device_ptr(out, dev, "out");
+  if (rc) return rc;
+  e = dqg::launch_silu_mul(gate_up, out, static_cast<int>(M), static_cast<int>(I),
+                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
+  return ok();
+}
+
 int dqg_device_status(int device, uint32_t* status, int reset) {
   if (status == nullptr) return fail(DQG_ERR_INVALID, "status must not be null");
   cudaError_t e = dqg::read_device_status(device, status, reset != 0);

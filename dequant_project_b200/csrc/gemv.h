@@ -129,4 +129,12 @@ cudaError_t read_device_status(int device, uint32_t* status, bool reset);
 
 cudaError_t launch_add_one(const float* x, float* out, int64_t n, cudaStream_t stream);
 
+// Decoder-step element-wise kernels (decode_ops.cu).
+cudaError_t launch_add_rms_norm(void* h, const void* delta, const void* w, void* y, int M, int H,
+                                float eps, cudaStream_t stream);
+cudaError_t launch_rope_kv_append(const void* qkv, const float* cosv, const float* sinv,
+                                  void* q_out, void* kc, void* vc, int M, int hq, int hkv, int D,
+                                  int pos, int cap, cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, cudaStream_t stream);
+
 }  // namespace dqg

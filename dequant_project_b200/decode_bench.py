@@ -1,0 +1,118 @@
+"""Decode ms/token of the tensor-parallel packed decoder.
+
+    python -m dequant_project_b200.decode_bench [--model llama2-7b] [--bits 4]
+        [--group-size 128] [--batch 1] [--kv-len 2048] [--steps 50] [--warmup 5]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
+        -m dequant_project_b200.decode_bench ...
+
+One process per GPU; the tensor-parallel width is the world size. The model
+(random N(0, 0.02) weights, every linear packed, N(0, 1) fp16 KV cache of
+``kv_len`` positions) is built on each rank, one decode step at position
+``kv_len`` is captured in a CUDA graph, and ``steps`` replays are timed with
+CUDA events on the replay stream after ``warmup`` untimed ones, bracketed by a
+barrier; the time is the maximum over ranks. Each replay rewrites the same
+cache slot, so every timed step does identical work. Rank 0 prints one JSON
+line: ms/token, tokens/s, and the step's bytes on one rank (packed weights, KV
+cache, embedding row, norms) over the time against the measured HBM copy
+bandwidth.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+
+MODELS = {"llama2-7b": "LLAMA2_7B", "llama3-70b": "LLAMA3_70B"}
+
+
+def run(args) -> dict | None:
+    from dequant_project_b200 import decoder as D
+    from dequant_project_b200.byte_model import measured_peaks
+    from dequant_project_b200.packer import QuantConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    cfg = getattr(D, MODELS[args.model])
+    if args.layers:
+        cfg = D.DecoderConfig(args.layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads,
+                              cfg.intermediate, cfg.vocab, cfg.rope_theta, cfg.eps)
+    q = QuantConfig(args.bits, args.group_size or None, args.sym)
+    dec = D.TPDecoder(cfg, q, world=world, rank=rank, device=dev, seed=args.seed,
+                      batch=args.batch, kv_len=args.kv_len)
+    torch.cuda.synchronize(dev)
+    gr = D.DecodeGraph(dec, args.kv_len)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        gr.replay()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        gr.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier(device_ids=[local])
+    by = dec.step_bytes(args.kv_len)
+    gr.release()
+    peaks = measured_peaks()
+    line = None
+    if rank == 0:
+        gbs = by["total"] / (ms * 1e-3) / 1e9
+        line = {
+            "metric": "decode ms/token", "value": round(ms, 4), "unit": "ms/token",
+            "tokens_per_s": round(args.batch / (ms * 1e-3), 1), "n_gpus": world,
+            "tp": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False,
+            "config": {"model": args.model, "layers": cfg.n_layers, "batch": args.batch,
+                       "kv_len": args.kv_len, "bits": args.bits,
+                       "group_size": args.group_size or "per-channel",
+                       "symmetric": args.sym, "lm_head": "packed, column-parallel"},
+            "data": "synthetic (random-init N(0,0.02) weights, N(0,1) fp16 KV cache)",
+            "bytes_per_rank": by,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "floor_ms": round(by["total"] / (peaks["hbm_gbs"] * 1e9) * 1e3, 4)},
+        }
+    if dist is not None:
+        dist.destroy_process_group()
+    return line
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--model", choices=sorted(MODELS), default="llama2-7b")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count")
+    ap.add_argument("--bits", type=int, default=4, choices=(2, 4, 8))
+    ap.add_argument("--group-size", type=int, default=128, help="0 = per-channel")
+    ap.add_argument("--sym", action="store_true")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--kv-len", type=int, default=2048)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+    line = run(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,88 @@
+"""Element-wise steps of the decoder around the packed GEMVs.
+
+CUDA tensors go through the sm_100a kernels of libdequant_b200.so
+(``dqg_add_rms_norm``, ``dqg_rope_kv_append``, ``dqg_silu_mul``) on torch's
+current stream; if the library is missing these calls raise. CPU tensors take
+the same formulas in torch: that branch exists for the host-logic tests of the
+tensor-parallel decoder (gloo ranks on the CPU) and is never taken for a CUDA
+tensor.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from dequant_project_b200 import _native
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def add_rms_norm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor,
+                 eps: float) -> torch.Tensor:
+    """If ``delta`` is given, ``h += delta`` in place (fp16); returns
+    RMSNorm(h) * weight as fp16 [M, H] (fp32 math)."""
+    if not h.is_cuda:
+        if delta is not None:
+            h.copy_(h + delta)
+        hf = h.float()
+        y = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)
+        return (y * weight.float()).to(torch.float16)
+    m, hd = h.shape
+    for t in (h, weight) + (() if delta is None else (delta,)):
+        if t.dtype != torch.float16 or not t.is_contiguous():
+            raise RuntimeError("add_rms_norm takes contiguous float16 tensors")
+    y = torch.empty_like(h)
+    _native.check(_native.lib().dqg_add_rms_norm(
+        h.data_ptr(), None if delta is None else delta.data_ptr(), weight.data_ptr(),
+        y.data_ptr(), m, hd, float(eps), _stream(h)))
+    return y
+
+
+def rope_kv_append(qkv: torch.Tensor, cos_row: torch.Tensor, sin_row: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, pos: int, n_q_heads: int,
+                   n_kv_heads: int) -> torch.Tensor:
+    """Rotate the query and key heads of ``qkv`` [M, (Hq + 2 Hkv) D] at one
+    position, write keys and values into slot ``pos`` of the caches
+    [M, Hkv, capacity, D]; returns the rotated queries [M, Hq, D]."""
+    m = qkv.shape[0]
+    d = k_cache.shape[-1]
+    if not qkv.is_cuda:
+        nq, nkv = n_q_heads * d, n_kv_heads * d
+
+        def rot(t):
+            tf = t.float()
+            h = d // 2
+            r = torch.cat([-tf[..., h:], tf[..., :h]], dim=-1)
+            return (tf * cos_row + r * sin_row).to(torch.float16)
+
+        q = rot(qkv[:, :nq].reshape(m, n_q_heads, d))
+        k_cache[:, :, pos] = rot(qkv[:, nq:nq + nkv].reshape(m, n_kv_heads, d))
+        v_cache[:, :, pos] = qkv[:, nq + nkv:].reshape(m, n_kv_heads, d)
+        return q
+    if not (qkv.is_contiguous() and k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("rope_kv_append takes contiguous tensors")
+    if cos_row.dtype != torch.float32 or sin_row.dtype != torch.float32:
+        raise RuntimeError("cos/sin rows must be float32")
+    q = torch.empty((m, n_q_heads, d), dtype=torch.float16, device=qkv.device)
+    _native.check(_native.lib().dqg_rope_kv_append(
+        qkv.data_ptr(), cos_row.data_ptr(), sin_row.data_ptr(), q.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), m, n_q_heads, n_kv_heads, d, pos,
+        k_cache.shape[2], _stream(qkv)))
+    return q
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """SwiGLU of ``gate_up`` [M, 2 I] (gate, then up) -> fp16 [M, I]."""
+    m, two_i = gate_up.shape
+    i = two_i // 2
+    if not gate_up.is_cuda:
+        return (F.silu(gate_up[:, :i].float()) * gate_up[:, i:].float()).to(torch.float16)
+    if not gate_up.is_contiguous() or gate_up.dtype != torch.float16:
+        raise RuntimeError("silu_mul takes a contiguous float16 tensor")
+    out = torch.empty((m, i), dtype=torch.float16, device=gate_up.device)
+    _native.check(_native.lib().dqg_silu_mul(gate_up.data_ptr(), out.data_ptr(), m, i,
+                                             _stream(gate_up)))
+    return out

@@ -1,0 +1,314 @@
+"""Tensor-parallel decode step of a Llama-architecture decoder whose linear
+layers are held packed (one process per GPU).
+
+The reference models this step only as bytes (KrishnaI2424/Dequant_Project
+``dequant/byte_model.py:179-251``: quantized projections and LM head, fp16 KV
+cache, one row of the embedding); this module runs it, with every linear layer
+going through the fused dequant + GEMV of this package:
+
+* per layer: RMSNorm -> QKV (column-parallel, this rank's query and KV heads
+  fused into one packed matrix) -> RoPE -> KV-cache append -> attention over
+  the cache -> O (row-parallel over the same heads, one all-reduce) ->
+  residual -> RMSNorm -> gate/up (column-parallel, fused) -> SwiGLU -> down
+  (row-parallel, one all-reduce) -> residual;
+* then the final RMSNorm and the LM head (column-parallel over the
+  vocabulary, quantized like the layers) whose slices are all-gathered.
+
+Weights are random N(0, 0.02) fp16 drawn per matrix from a seeded generator on
+the model's device, quantized with the packer and then sharded with
+``tensor_parallel``, so every tensor-parallel width holds exactly the packed
+codes, scales and zero-points of the single-GPU model. Norm weights are ones
+(Llama's initialisation); the KV cache of the first ``kv_len`` positions is
+N(0, 1) fp16.
+
+``DecodeGraph`` captures one step at a fixed position into a CUDA graph (the
+collectives included) for timing; eager ``step`` takes any position.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.nn.functional as F
+
+from dequant_project_b200 import decode_ops as ops
+from dequant_project_b200.packer import PackedWeight, QuantConfig, quantize_tensor
+from dequant_project_b200.tensor_parallel import (intermediate_bounds, shard_columns,
+                                                  shard_rows, split_bounds)
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    """Architecture of a Llama-style decoder."""
+
+    n_layers: int
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    intermediate: int
+    vocab: int
+    rope_theta: float = 10000.0
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.n_heads
+
+
+LLAMA2_7B = DecoderConfig(32, 4096, 32, 32, 11008, 32000)
+LLAMA3_70B = DecoderConfig(80, 8192, 64, 8, 28672, 128256, rope_theta=500000.0)
+
+
+def cat_rows(parts: list[PackedWeight]) -> PackedWeight:
+    """Row-wise concatenation of packed weights of one format and K (the rows
+    of each part keep their own scales and zero-points)."""
+    cfg, k = parts[0].config, parts[0].shape[1]
+    if any(p.config != cfg or p.shape[1] != k for p in parts):
+        raise ValueError("cat_rows needs parts of one format and one K")
+    zeros = None if parts[0].zeros is None else torch.cat([p.zeros for p in parts])
+    return PackedWeight(qweight=torch.cat([p.qweight for p in parts]),
+                        scales=torch.cat([p.scales for p in parts]), zeros=zeros,
+                        config=cfg, shape=(sum(p.shape[0] for p in parts), k))
+
+
+def rope_tables(head_dim: int, theta: float, positions: int, device) -> tuple:
+    """cos/sin [positions, head_dim] (fp32) of the rotate-half RoPE."""
+    inv = theta ** (-torch.arange(0, head_dim, 2, dtype=torch.float64, device=device) / head_dim)
+    ang = torch.arange(positions, dtype=torch.float64, device=device)[:, None] * inv[None, :]
+    ang = torch.cat([ang, ang], dim=-1)
+    return ang.cos().float(), ang.sin().float()
+
+
+def attention(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor) -> torch.Tensor:
+    """One query per sequence and head over the cache.
+
+    q [M, Hq, D] fp16; kc, vc [M, Hkv, T, D] fp16 (T = positions to attend).
+    Returns [M, Hq, D] fp16. On the GPU this is torch's fused
+    scaled-dot-product attention (grouped KV heads); elsewhere an fp32
+    softmax(q k^T / sqrt(D)) v."""
+    m, hq, d = q.shape
+    hkv = kc.shape[1]
+    if q.is_cuda:
+        o = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=hq != hkv)
+        return o.squeeze(2)
+    g = hq // hkv
+    qf = q.float().view(m, hkv, g, d)
+    s = torch.einsum("mkgd,mktd->mkgt", qf, kc.float()) / math.sqrt(d)
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("mkgt,mktd->mkgd", p, vc.float()).reshape(m, hq, d).to(torch.float16)
+
+
+def _default_linear(x: torch.Tensor, pw: PackedWeight) -> torch.Tensor:
+    from dequant_project_b200 import quant_linear as ql
+    if x.shape[0] <= ql.MAX_M:
+        return ql.gemv(x, pw)
+    return F.linear(x, ql.dequantize_cuda(pw))
+
+
+class TPDecoder:
+    """This rank's shard of a packed decoder, plus its KV cache.
+
+    ``world``/``rank``/``group`` describe the tensor-parallel process group
+    (``world == 1``: no collectives). Query and KV heads split evenly over the
+    ranks (both counts must divide by ``world``); the MLP's intermediate
+    dimension splits on quantization-group boundaries
+    (``intermediate_bounds``), the vocabulary evenly to within one row.
+    ``linear_fn(x, pw)`` replaces the GEMV (tests run the host logic on the
+    CPU with a dequantize-then-matmul stand-in)."""
+
+    def __init__(self, cfg: DecoderConfig, qcfg: QuantConfig, *, world: int = 1, rank: int = 0,
+                 group=None, device=None, seed: int = 0, batch: int = 1, kv_len: int = 2048,
+                 max_new: int = 1, quantize_lm_head: bool = True,
+                 linear_fn: Callable | None = None):
+        if cfg.n_heads % world or cfg.n_kv_heads % world:
+            raise ValueError(f"{cfg.n_heads} query / {cfg.n_kv_heads} KV heads do not split "
+                             f"over {world} ranks")
+        if cfg.n_heads % cfg.n_kv_heads:
+            raise ValueError("query heads must be a multiple of KV heads")
+        self.cfg, self.qcfg = cfg, qcfg
+        self.world, self.rank, self.group = world, rank, group
+        self.device = torch.device(device) if device is not None else torch.device("cpu")
+        self.batch, self.kv_len = batch, kv_len
+        self.capacity = kv_len + max_new
+        self._linear = linear_fn or _default_linear
+        d = cfg.head_dim
+        self.hq = cfg.n_heads // world
+        self.hkv = cfg.n_kv_heads // world
+        gen = torch.Generator(device=self.device)
+
+        def weight(shape, idx):
+            gen.manual_seed(seed * 1_000_003 + idx)
+            w = torch.randn(shape, generator=gen, device=self.device, dtype=torch.float32)
+            return (w * 0.02).to(torch.float16)
+
+        def packed(shape, idx):
+            return quantize_tensor(weight(shape, idx), qcfg)
+
+        q_bounds = [b * self.hq * d for b in range(world + 1)]
+        kv_bounds = [b * self.hkv * d for b in range(world + 1)]
+        self.inter_bounds = intermediate_bounds(cfg.intermediate, qcfg, world)
+        self.vocab_bounds = split_bounds(cfg.vocab, world)
+        self.layers = []
+        for layer in range(cfg.n_layers):
+            base = 16 * (layer + 1)
+            wq = packed((cfg.n_heads * d, cfg.hidden), base + 0)
+            wk = packed((cfg.n_kv_heads * d, cfg.hidden), base + 1)
+            wv = packed((cfg.n_kv_heads * d, cfg.hidden), base + 2)
+            qkv = cat_rows([shard_columns(wq, world, rank, q_bounds),
+                            shard_columns(wk, world, rank, kv_bounds),
+                            shard_columns(wv, world, rank, kv_bounds)])
+            del wq, wk, wv
+            wo = packed((cfg.hidden, cfg.n_heads * d), base + 3)
+            o, _, _ = shard_rows(wo, world, rank, q_bounds)
+            del wo
+            wg = packed((cfg.intermediate, cfg.hidden), base + 4)
+            wu = packed((cfg.intermediate, cfg.hidden), base + 5)
+            gu = cat_rows([shard_columns(wg, world, rank, self.inter_bounds),
+                           shard_columns(wu, world, rank, self.inter_bounds)])
+            del wg, wu
+            wd = packed((cfg.hidden, cfg.intermediate), base + 6)
+            down, _, _ = shard_rows(wd, world, rank, self.inter_bounds)
+            del wd
+            self.layers.append({"qkv": qkv, "o": o, "gu": gu, "down": down})
+        self.ir = self.inter_bounds[rank + 1] - self.inter_bounds[rank]
+        self.embed = weight((cfg.vocab, cfg.hidden), 1)
+        head = weight((cfg.vocab, cfg.hidden), 2)
+        lo, hi = self.vocab_bounds[rank], self.vocab_bounds[rank + 1]
+        if quantize_lm_head:
+            self.lm_head = shard_columns(quantize_tensor(head, qcfg), world, rank,
+                                         self.vocab_bounds)
+        else:
+            self.lm_head = head[lo:hi].contiguous()
+        del head
+        ones = torch.ones(cfg.hidden, dtype=torch.float16, device=self.device)
+        self.attn_norm = [ones] * cfg.n_layers
+        self.mlp_norm = [ones] * cfg.n_layers
+        self.final_norm = ones
+        self.cos, self.sin = rope_tables(d, cfg.rope_theta, self.capacity, self.device)
+        self.reset_cache(seed)
+
+    # ------------------------------------------------------------------ cache
+    def reset_cache(self, seed: int = 0) -> None:
+        """KV cache [batch, kv heads of this rank, capacity, head_dim] per
+        layer; positions < kv_len are N(0, 1) fp16 (this rank's heads of the
+        full cache, so every tensor-parallel width sees the same values)."""
+        cfg, d = self.cfg, self.cfg.head_dim
+        gen = torch.Generator(device=self.device)
+        self.k_cache, self.v_cache = [], []
+        h0 = self.rank * self.hkv
+        for layer in range(cfg.n_layers):
+            for which, dst in ((0, self.k_cache), (1, self.v_cache)):
+                gen.manual_seed(seed * 7_919 + 2 * layer + which + 1)
+                full = torch.randn((self.batch, cfg.n_kv_heads, self.kv_len, d), generator=gen,
+                                   device=self.device, dtype=torch.float32).to(torch.float16)
+                c = torch.zeros((self.batch, self.hkv, self.capacity, d), dtype=torch.float16,
+                                device=self.device)
+                c[:, :, :self.kv_len] = full[:, h0:h0 + self.hkv]
+                dst.append(c)
+
+    # -------------------------------------------------------------- forward
+    def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def _lm_head(self, x: torch.Tensor) -> torch.Tensor:
+        if isinstance(self.lm_head, PackedWeight):
+            return self._linear(x, self.lm_head)
+        return F.linear(x, self.lm_head)
+
+    def step(self, tokens: torch.Tensor, pos: int) -> torch.Tensor:
+        """One decode step: tokens [batch] int64 at position ``pos`` (their K/V
+        go to cache slot ``pos``, attention covers positions 0..pos). Returns
+        the full logits [batch, vocab] fp16 on every rank.
+
+        Per layer five kernels surround the three packed GEMVs and the two
+        all-reduces: residual add + RMSNorm (the residual of the previous
+        block folded in), RoPE + KV append, attention, residual add + RMSNorm,
+        SwiGLU."""
+        cfg, d = self.cfg, self.cfg.head_dim
+        if not 0 <= pos < self.capacity:
+            raise ValueError(f"position {pos} outside the cache (capacity {self.capacity})")
+        m = tokens.shape[0]
+        if m != self.batch:
+            raise ValueError(f"expected {self.batch} tokens, got {m}")
+        h = self.embed[tokens]
+        cos, sin = self.cos[pos], self.sin[pos]
+        nq = self.hq * d
+        pending = None
+        for layer, w in enumerate(self.layers):
+            x = ops.add_rms_norm(h, pending, self.attn_norm[layer], cfg.eps)
+            qkv = self._linear(x, w["qkv"])
+            kc, vc = self.k_cache[layer], self.v_cache[layer]
+            q = ops.rope_kv_append(qkv, cos, sin, kc, vc, pos, self.hq, self.hkv)
+            a = attention(q, kc[:, :, :pos + 1], vc[:, :, :pos + 1])
+            o = self._all_reduce(self._linear(a.reshape(m, nq), w["o"]))
+            x = ops.add_rms_norm(h, o, self.mlp_norm[layer], cfg.eps)
+            act = ops.silu_mul(self._linear(x, w["gu"]))
+            pending = self._all_reduce(self._linear(act, w["down"]))
+        x = ops.add_rms_norm(h, pending, self.final_norm, cfg.eps)
+        logits = self._lm_head(x)
+        if self.world == 1:
+            return logits
+        import torch.distributed as dist
+        width = max(b - a for a, b in zip(self.vocab_bounds[:-1], self.vocab_bounds[1:]))
+        padded = logits.new_zeros((m, width))
+        padded[:, :logits.shape[1]] = logits
+        parts = [torch.empty_like(padded) for _ in range(self.world)]
+        dist.all_gather(parts, padded, group=self.group)
+        return torch.cat([p[:, :b - a] for p, a, b in
+                          zip(parts, self.vocab_bounds[:-1], self.vocab_bounds[1:])], dim=1)
+
+    def packed_bytes(self) -> int:
+        """Bytes of this rank's packed weights (layers and LM head)."""
+        n = sum(pw.nbytes for w in self.layers for pw in w.values())
+        head = self.lm_head
+        return n + (head.nbytes if isinstance(head, PackedWeight) else head.numel() * 2)
+
+    def step_bytes(self, pos: int) -> dict:
+        """Bytes one step at ``pos`` must move on this rank (the terms of the
+        reference's decode byte model, dequant/byte_model.py:179-251, for this
+        rank's shard): packed weights and LM head, the KV cache read for
+        positions 0..pos and the new slot written, the embedding row, norm
+        weights; activations (a few KB) are left out."""
+        cfg, d = self.cfg, self.cfg.head_dim
+        kv_read = cfg.n_layers * 2 * self.batch * self.hkv * (pos + 1) * d * 2
+        kv_write = cfg.n_layers * 2 * self.batch * self.hkv * d * 2
+        out = {"weights": self.packed_bytes(), "kv_cache": kv_read + kv_write,
+               "embedding": self.batch * cfg.hidden * 2,
+               "norms": (2 * cfg.n_layers + 1) * cfg.hidden * 2}
+        out["total"] = sum(out.values())
+        return out
+
+
+class DecodeGraph:
+    """One decode step at a fixed position, captured in a CUDA graph on this
+    rank (GEMVs, attention and the collectives). ``replay()`` reruns it on the
+    current contents of ``tokens``; ``logits`` holds the output."""
+
+    def __init__(self, dec: TPDecoder, pos: int, warmup: int = 2):
+        self.dec, self.pos = dec, pos
+        self.tokens = torch.zeros(dec.batch, dtype=torch.int64, device=dec.device)
+        self.stream = torch.cuda.Stream(device=dec.device)
+        self.stream.wait_stream(torch.cuda.current_stream(dec.device))
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                dec.step(self.tokens, pos)
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.logits = dec.step(self.tokens, pos)
+        self.stream.synchronize()
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.logits
+
+    def release(self) -> None:
+        """Drop the graph (before the process group is destroyed)."""
+        self.graph.reset()
+        self.graph = None

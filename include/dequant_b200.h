@@ -88,6 +88,39 @@ int dqg_dequantize(const int32_t *qweight, const void *scales, const void *zeros
  */
 int dqg_device_status(int device, uint32_t *status, int reset);
 
+/*
+ * Element-wise steps of the tensor-parallel decoder around the GEMVs
+ * (dequant_project_b200/decoder.py). No reference counterpart: the reference
+ * only models the decode step as bytes (dequant/byte_model.py:179-251). fp16
+ * tensors, row-major, on the current device.
+ */
+
+/*
+ * Residual add + RMSNorm over rows of H values (H % 8 == 0, all pointers
+ * 16-byte aligned): if delta != NULL, h[m] = fp16(h[m] + delta[m]) in place;
+ * then y[m] = fp16((h[m] * rsqrt(mean(h[m]^2) + eps)) * weight), fp32 math.
+ */
+int dqg_add_rms_norm(void *h, const void *delta, const void *weight, void *y, int64_t M,
+                     int64_t H, float eps, void *stream);
+
+/*
+ * Rotate-half RoPE at one position and KV-cache append. qkv is [M, (Hq +
+ * 2 Hkv) * D] (query heads, then key heads, then value heads); cos_row and
+ * sin_row are fp32 [D] for the position. Rotated queries go to q_out
+ * [M, Hq, D]; rotated keys and the values go to slot `pos` of k_cache and
+ * v_cache [M, Hkv, capacity, D].
+ */
+int dqg_rope_kv_append(const void *qkv, const float *cos_row, const float *sin_row, void *q_out,
+                       void *k_cache, void *v_cache, int64_t M, int64_t n_q_heads,
+                       int64_t n_kv_heads, int64_t head_dim, int64_t pos, int64_t capacity,
+                       void *stream);
+
+/*
+ * SwiGLU: gate_up is [M, 2 I] (gate columns, then up columns);
+ * out[m, i] = fp16(silu(gate) * up), silu(g) = g / (1 + exp(-g)) in fp32.
+ */
+int dqg_silu_mul(const void *gate_up, void *out, int64_t M, int64_t I, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

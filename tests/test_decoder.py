@@ -1,0 +1,152 @@
+"""Tensor-parallel decoder step: host logic on the CPU.
+
+The decoder's linear layers run through a CPU stand-in for the GEMV (the
+reference CPU path, x @ packer.dequantize(W)^T in fp32, fp16 out) and its
+element-wise steps through the torch formulas of ``decode_ops``. Checked here:
+the single-rank step against an independent fp32 restatement of a Llama decode
+step (loops over heads, no fused steps), two gloo ranks against one rank
+(head split, intermediate split on group boundaries, the two all-reduces per
+layer, the vocabulary all-gather), and the argument checks.
+"""
+
+from __future__ import annotations
+
+import math
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from dequant_project_b200.decoder import DecoderConfig, TPDecoder, cat_rows
+from dequant_project_b200.packer import QuantConfig, dequantize, quantize_tensor
+
+TINY = DecoderConfig(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640,
+                     vocab=1000)
+QCFG = QuantConfig(4, 64, False)
+
+
+def cpu_linear(x, pw):
+    w = dequantize(pw).float()
+    return (x.float() @ w.t()).to(torch.float16)
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def reference_step(dec: TPDecoder, tokens, pos):
+    """fp32 Llama decode step from the decoder's own (world 1) weights and
+    caches, written out per head; returns logits [M, vocab] fp32."""
+    cfg, d = dec.cfg, dec.cfg.head_dim
+    m = tokens.shape[0]
+    h = dec.embed[tokens].float()
+    inv = cfg.rope_theta ** (-torch.arange(0, d, 2, dtype=torch.float64) / d)
+    ang = pos * inv
+    cos = torch.cat([ang.cos(), ang.cos()]).float()
+    sin = torch.cat([ang.sin(), ang.sin()]).float()
+
+    def norm(x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.eps)
+
+    def rope(t):
+        half = d // 2
+        return t * cos + torch.cat([-t[..., half:], t[..., :half]], dim=-1) * sin
+
+    nq, nkv = cfg.n_heads * d, cfg.n_kv_heads * d
+    group = cfg.n_heads // cfg.n_kv_heads
+    for layer, w in enumerate(dec.layers):
+        qkv = norm(h) @ dequantize(w["qkv"]).float().t()
+        q = rope(qkv[:, :nq].reshape(m, cfg.n_heads, d))
+        k = rope(qkv[:, nq:nq + nkv].reshape(m, cfg.n_kv_heads, d))
+        v = qkv[:, nq + nkv:].reshape(m, cfg.n_kv_heads, d)
+        kc = dec.k_cache[layer][:, :, :pos].float()
+        vc = dec.v_cache[layer][:, :, :pos].float()
+        out = torch.empty(m, cfg.n_heads, d)
+        for b in range(m):
+            for hh in range(cfg.n_heads):
+                kv = hh // group
+                keys = torch.cat([kc[b, kv], k[b, kv][None]])
+                vals = torch.cat([vc[b, kv], v[b, kv][None]])
+                p = torch.softmax(keys @ q[b, hh] / math.sqrt(d), dim=0)
+                out[b, hh] = p @ vals
+        h = h + out.reshape(m, nq) @ dequantize(w["o"]).float().t()
+        gu = norm(h) @ dequantize(w["gu"]).float().t()
+        i = cfg.intermediate
+        act = torch.nn.functional.silu(gu[:, :i]) * gu[:, i:]
+        h = h + act @ dequantize(w["down"]).float().t()
+    return norm(h) @ dequantize(dec.lm_head).float().t()
+
+
+def test_single_rank_matches_fp32_reference():
+    dec = TPDecoder(TINY, QCFG, seed=3, batch=2, kv_len=24, linear_fn=cpu_linear)
+    tokens = torch.tensor([5, 977])
+    pos = dec.kv_len
+    ref = reference_step(dec, tokens, pos)        # reads the cache before the step writes it
+    logits = dec.step(tokens, pos).float()
+    err = (logits - ref).abs().max() / ref.abs().max()
+    assert err < 1e-2, err
+
+
+def test_step_writes_cache_slot_and_is_repeatable():
+    dec = TPDecoder(TINY, QCFG, seed=1, batch=1, kv_len=8, max_new=2, linear_fn=cpu_linear)
+    before = [c.clone() for c in dec.k_cache]
+    tok = torch.tensor([7])
+    a = dec.step(tok, 8)
+    for layer, c in enumerate(dec.k_cache):
+        assert torch.equal(c[:, :, :8], before[layer][:, :, :8])
+        assert c[:, :, 8].abs().sum() > 0 and torch.equal(c[:, :, 9], before[layer][:, :, 9])
+    assert torch.equal(dec.step(tok, 8), a)       # same slot rewritten with the same values
+    with pytest.raises(ValueError, match="outside the cache"):
+        dec.step(tok, 10)
+
+
+def test_cat_rows_is_row_concatenation():
+    torch.manual_seed(0)
+    parts = [quantize_tensor(torch.randn(n, 256, dtype=torch.float16) * 0.02, QCFG)
+             for n in (64, 32, 96)]
+    cat = cat_rows(parts)
+    assert cat.shape == (192, 256)
+    assert torch.equal(dequantize(cat), torch.cat([dequantize(p) for p in parts]))
+    with pytest.raises(ValueError):
+        cat_rows([parts[0], quantize_tensor(torch.randn(8, 128, dtype=torch.float16), QCFG)])
+
+
+def test_rejects_head_counts_that_do_not_split():
+    with pytest.raises(ValueError, match="do not split"):
+        TPDecoder(TINY, QCFG, world=3, linear_fn=cpu_linear)
+
+
+def test_gloo_two_ranks_match_one_rank():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    import tp_workers
+    procs = [ctx.Process(target=tp_workers.decoder_step, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out, t0 = {}, time.time()
+    while len(out) < world and time.time() - t0 < 240:
+        try:
+            r, status, val = q.get(timeout=1)
+            out[r] = (status, val)
+        except Exception:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert set(out) == {0, 1}, out
+    for r, (status, val) in out.items():
+        assert status == "ok", val
+    assert torch.equal(out[0][1], out[1][1])
+    one = TPDecoder(TINY, QCFG, seed=3, batch=2, kv_len=24, linear_fn=cpu_linear)
+    ref = one.step(torch.tensor([5, 977]), one.kv_len).float()
+    err = (out[0][1].float() - ref).abs().max() / ref.abs().max()
+    assert err < 5e-3, err

@@ -1,0 +1,147 @@
+"""Decoder step on the GPU: the element-wise kernels against torch's formulas,
+the packed-GEMV decoder against the same decoder with dequantize-then-matmul
+linears, CUDA-graph replay against eager, and two NCCL ranks against one GPU.
+"""
+
+from __future__ import annotations
+
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")]
+
+from dequant_project_b200 import decode_ops  # noqa: E402
+from dequant_project_b200.decoder import DecodeGraph, DecoderConfig, TPDecoder  # noqa: E402
+from dequant_project_b200.packer import QuantConfig  # noqa: E402
+
+SMALL = DecoderConfig(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=4, intermediate=2816,
+                      vocab=5000)
+FORMATS = [(4, 128, False), (2, 64, False), (8, None, True)]
+
+
+def dequant_linear(x, pw):
+    from dequant_project_b200.quant_linear import dequantize_cuda
+    return (x.float() @ dequantize_cuda(pw).float().t()).to(torch.float16)
+
+
+def test_add_rms_norm_matches_torch():
+    g = torch.Generator(device="cuda").manual_seed(0)
+    m, hd = 3, 4096
+    h = torch.randn(m, hd, generator=g, device="cuda").half()
+    delta = torch.randn(m, hd, generator=g, device="cuda").half()
+    w = (1 + 0.1 * torch.randn(hd, generator=g, device="cuda")).half()
+    h_ref = h + delta
+    hf = h_ref.float()
+    y_ref = ((hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5)) * w.float()).half()
+    y = decode_ops.add_rms_norm(h, delta, w, 1e-5)
+    assert torch.equal(h, h_ref)                       # the residual add is one fp16 rounding
+    torch.testing.assert_close(y, y_ref, rtol=2e-3, atol=1e-3)
+    y2 = decode_ops.add_rms_norm(h, None, w, 1e-5)     # no residual: h unchanged
+    assert torch.equal(h, h_ref)
+    torch.testing.assert_close(y2, y_ref, rtol=2e-3, atol=1e-3)
+
+
+def test_rope_kv_append_matches_torch_formula():
+    g = torch.Generator(device="cuda").manual_seed(1)
+    m, hq, hkv, d, cap, pos = 2, 8, 2, 128, 40, 33
+    qkv = torch.randn(m, (hq + 2 * hkv) * d, generator=g, device="cuda").half()
+    ang = torch.rand(d // 2, generator=g, device="cuda") * 30
+    cos = torch.cat([ang.cos(), ang.cos()]).float()
+    sin = torch.cat([ang.sin(), ang.sin()]).float()
+    kc = torch.randn(m, hkv, cap, d, generator=g, device="cuda").half()
+    vc = torch.randn(m, hkv, cap, d, generator=g, device="cuda").half()
+    kc0, vc0 = kc.clone(), vc.clone()
+
+    def rot(t):
+        tf = t.float()
+        r = torch.cat([-tf[..., d // 2:], tf[..., :d // 2]], dim=-1)
+        return (tf * cos + r * sin).half()
+
+    q = decode_ops.rope_kv_append(qkv, cos, sin, kc, vc, pos, hq, hkv)
+    nq, nkv = hq * d, hkv * d
+    assert torch.equal(q, rot(qkv[:, :nq].reshape(m, hq, d)))
+    assert torch.equal(kc[:, :, pos], rot(qkv[:, nq:nq + nkv].reshape(m, hkv, d)))
+    assert torch.equal(vc[:, :, pos], qkv[:, nq + nkv:].reshape(m, hkv, d))
+    others = [t for t in range(cap) if t != pos]
+    assert torch.equal(kc[:, :, others], kc0[:, :, others])
+    assert torch.equal(vc[:, :, others], vc0[:, :, others])
+
+
+def test_silu_mul_matches_torch():
+    g = torch.Generator(device="cuda").manual_seed(2)
+    gu = (3 * torch.randn(5, 2 * 2816, generator=g, device="cuda")).half()
+    ref = (F.silu(gu[:, :2816].float()) * gu[:, 2816:].float()).half()
+    torch.testing.assert_close(decode_ops.silu_mul(gu), ref, rtol=1e-3, atol=1e-4)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("batch", (1, 8))
+def test_decoder_matches_dequantized_reference(fmt, batch):
+    bits, gs, sym = fmt
+    q = QuantConfig(bits, gs, sym)
+    dec = TPDecoder(SMALL, q, device="cuda", seed=5, batch=batch, kv_len=100)
+    ref = TPDecoder(SMALL, q, device="cuda", seed=5, batch=batch, kv_len=100,
+                    linear_fn=dequant_linear)
+    tokens = torch.arange(batch, device="cuda") * 611 % SMALL.vocab
+    a = dec.step(tokens, 100).float()
+    b = ref.step(tokens, 100).float()
+    err = ((a - b).abs().max() / b.abs().max()).item()
+    assert err < 1e-2, err
+
+
+def test_graph_replay_matches_eager():
+    dec = TPDecoder(SMALL, QuantConfig(4, 128, False), device="cuda", seed=6, batch=1,
+                    kv_len=64)
+    tokens = torch.tensor([17], device="cuda")
+    eager = dec.step(tokens, 64).clone()
+    gr = DecodeGraph(dec, 64)
+    gr.tokens.copy_(tokens)
+    out = gr.replay().clone()
+    torch.cuda.synchronize()
+    gr.release()
+    assert torch.equal(out, eager)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_two_ranks_match_one_gpu():
+    import tp_workers
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=tp_workers.decoder_step_nccl, args=(r, 2, port, q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    out, t0 = {}, time.time()
+    while len(out) < 2 and time.time() - t0 < 300:
+        try:
+            r, status, val = q.get(timeout=1)
+            out[r] = (status, val)
+        except Exception:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert set(out) == {0, 1}, out
+    for r, (status, val) in out.items():
+        assert status == "ok", val
+    one = TPDecoder(SMALL, QuantConfig(4, 128, False), device="cuda", seed=5, batch=2,
+                    kv_len=100)
+    ref = one.step(torch.tensor([3, 4001], device="cuda"), 100).float().cpu()
+    for r in (0, 1):
+        err = ((out[r][1].float() - ref).abs().max() / ref.abs().max()).item()
+        assert err < 5e-3, err

@@ -80,3 +80,50 @@ def tp_rank_fails(rank, world, port, queue):
         queue.put((rank, "completed", None, None))
     except Exception as exc:
         queue.put((rank, "error", f"{type(exc).__name__}: {exc}", None))
+
+
+def decoder_step(rank, world, port, queue):
+    """One decode step of the tiny test decoder on this gloo rank."""
+    try:
+        from dequant_project_b200.decoder import DecoderConfig, TPDecoder
+        from dequant_project_b200.packer import QuantConfig
+        dist = _init(rank, world, port, "gloo", 60)
+        cfg = DecoderConfig(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640,
+                            vocab=1000)
+        dec = TPDecoder(cfg, QuantConfig(4, 64, False), world=world, rank=rank, seed=3, batch=2,
+                        kv_len=24, linear_fn=_cpu_linear)
+        out = dec.step(torch.tensor([5, 977]), dec.kv_len)
+        queue.put((rank, "ok", out))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        queue.put((rank, "error", traceback.format_exc()))
+
+
+def decoder_step_nccl(rank, world, port, queue):
+    """One decode step of the small GPU test decoder on this NCCL rank (one GPU
+    per rank), eager and then replayed from a CUDA graph."""
+    try:
+        from dequant_project_b200.decoder import DecodeGraph, DecoderConfig, TPDecoder
+        from dequant_project_b200.packer import QuantConfig
+        dist = _init(rank, world, port, "nccl", 60)
+        cfg = DecoderConfig(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=4,
+                            intermediate=2816, vocab=5000)
+        dev = torch.device("cuda", rank)
+        dec = TPDecoder(cfg, QuantConfig(4, 128, False), world=world, rank=rank, device=dev,
+                        seed=5, batch=2, kv_len=100)
+        tokens = torch.tensor([3, 4001], device=dev)
+        eager = dec.step(tokens, 100).clone()
+        gr = DecodeGraph(dec, 100)
+        gr.tokens.copy_(tokens)
+        replayed = gr.replay().clone()
+        torch.cuda.synchronize(dev)
+        gr.release()
+        err = ((replayed.float() - eager.float()).abs().max() / eager.float().abs().max()).item()
+        if err > 1e-3:
+            raise AssertionError(f"graph replay differs from the eager step (rel {err})")
+        queue.put((rank, "ok", eager.cpu()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        queue.put((rank, "error", traceback.format_exc()))
