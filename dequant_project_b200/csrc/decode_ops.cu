@@ -3,10 +3,17 @@
 // small torch kernels with one launch; all are tiny next to the GEMVs (a
 // decode step moves kilobytes through them) and are bound by launch latency,
 // so each is a single pass with one CTA per row or per head.
+//
+// All three are launched with programmatic dependent launch and wait for the
+// previous grid (griddepcontrol.wait) before touching memory, then at once let
+// the next grid launch: a GEMV that follows can be scheduled and run its own
+// set-up while one of these runs, and one of these can be scheduled while a
+// GEMV runs, so their launch latencies overlap instead of adding up.
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "common.cuh"
 #include "gemv.h"
 
 namespace dqg {
@@ -22,6 +29,8 @@ __device__ __forceinline__ float h2f(__half v) { return __half2float(v); }
 __global__ void __launch_bounds__(kNormThreads)
     add_rms_norm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
                         const __half* __restrict__ w, __half* __restrict__ y, int H, float eps) {
+  pdl_wait_prior_grid();
+  pdl_launch_dependents();
   const int m = blockIdx.x;
   __half* hr = h + static_cast<int64_t>(m) * H;
   const __half* dr = delta ? delta + static_cast<int64_t>(m) * H : nullptr;
@@ -77,6 +86,8 @@ __global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const floa
                                       const float* __restrict__ sinv, __half* __restrict__ q_out,
                                       __half* __restrict__ kc, __half* __restrict__ vc, int hq,
                                       int hkv, int D, int pos, int cap) {
+  pdl_wait_prior_grid();
+  pdl_launch_dependents();
   const int m = blockIdx.x;
   const int hd = blockIdx.y;
   const int half = D / 2;
@@ -108,6 +119,8 @@ __global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const floa
 // silu(g) = g / (1 + exp(-g)) in fp32.
 __global__ void silu_mul_kernel(const __half* __restrict__ gu, __half* __restrict__ out, int I,
                                 int64_t total) {
+  pdl_wait_prior_grid();
+  pdl_launch_dependents();
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t m = e / I;
@@ -121,23 +134,37 @@ __global__ void silu_mul_kernel(const __half* __restrict__ gu, __half* __restric
 
 }  // namespace
 
+// Launch with the programmatic-stream-serialization attribute (see top).
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, int threads, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
 cudaError_t launch_add_rms_norm(void* h, const void* delta, const void* w, void* y, int M, int H,
                                 float eps, cudaStream_t stream) {
-  add_rms_norm_kernel<<<M, kNormThreads, 0, stream>>>(
-      static_cast<__half*>(h), static_cast<const __half*>(delta), static_cast<const __half*>(w),
-      static_cast<__half*>(y), H, eps);
-  return cudaGetLastError();
+  return launch_pdl(add_rms_norm_kernel, dim3(M), kNormThreads, stream, static_cast<__half*>(h),
+                    static_cast<const __half*>(delta), static_cast<const __half*>(w),
+                    static_cast<__half*>(y), H, eps);
 }
 
 cudaError_t launch_rope_kv_append(const void* qkv, const float* cosv, const float* sinv,
                                   void* q_out, void* kc, void* vc, int M, int hq, int hkv, int D,
                                   int pos, int cap, cudaStream_t stream) {
-  const dim3 grid(M, hq + hkv);
   const int threads = D / 2 < 32 ? 32 : (D / 2 > 256 ? 256 : D / 2);
-  rope_kv_append_kernel<<<grid, threads, 0, stream>>>(
-      static_cast<const __half*>(qkv), cosv, sinv, static_cast<__half*>(q_out),
-      static_cast<__half*>(kc), static_cast<__half*>(vc), hq, hkv, D, pos, cap);
-  return cudaGetLastError();
+  return launch_pdl(rope_kv_append_kernel, dim3(M, hq + hkv), threads, stream,
+                    static_cast<const __half*>(qkv), cosv, sinv, static_cast<__half*>(q_out),
+                    static_cast<__half*>(kc), static_cast<__half*>(vc), hq, hkv, D, pos, cap);
 }
 
 cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, cudaStream_t stream) {
@@ -145,9 +172,8 @@ cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, cudaStream_
   const int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
   if (blocks > 4 * 148) blocks = 4 * 148;
-  silu_mul_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
-      static_cast<const __half*>(gu), static_cast<__half*>(out), I, total);
-  return cudaGetLastError();
+  return launch_pdl(silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), threads, stream,
+                    static_cast<const __half*>(gu), static_cast<__half*>(out), I, total);
 }
 
 }  // namespace dqg
