@@ -21,6 +21,10 @@ codes, scales and zero-points of the single-GPU model. Norm weights are ones
 (Llama's initialisation); the KV cache of the first ``kv_len`` positions is
 N(0, 1) fp16.
 
+``PackedModel`` holds the full packed weights of a model (the same values the
+seeded construction produces) and saves/loads them in the ``packed_io``
+format, so a large model is quantized once and then only loaded.
+
 ``DecodeGraph`` captures one step at a fixed position into a CUDA graph (the
 collectives included) for timing; eager ``step`` takes any position.
 """
@@ -108,6 +112,104 @@ def _default_linear(x: torch.Tensor, pw: PackedWeight) -> torch.Tensor:
     return F.linear(x, ql.dequantize_cuda(pw))
 
 
+LAYER_MATRICES = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def layer_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
+    """[N, K] of each linear layer of one decoder layer (full, unsharded)."""
+    d = cfg.head_dim
+    return {"q": (cfg.n_heads * d, cfg.hidden), "k": (cfg.n_kv_heads * d, cfg.hidden),
+            "v": (cfg.n_kv_heads * d, cfg.hidden), "o": (cfg.hidden, cfg.n_heads * d),
+            "gate": (cfg.intermediate, cfg.hidden), "up": (cfg.intermediate, cfg.hidden),
+            "down": (cfg.hidden, cfg.intermediate)}
+
+
+class SeededWeights:
+    """Random N(0, 0.02) fp16 weights, one seeded draw per matrix on
+    ``device``, quantized on request (the default weight source)."""
+
+    def __init__(self, qcfg: QuantConfig, seed: int, device):
+        self.qcfg, self.seed, self.device = qcfg, seed, device
+        self.gen = torch.Generator(device=device)
+
+    def _index(self, name: str) -> int:
+        if name == "embed":
+            return 1
+        if name == "lm_head":
+            return 2
+        _, layer, mat = name.split(".")
+        return 16 * (int(layer) + 1) + LAYER_MATRICES.index(mat)
+
+    def tensor(self, name: str, shape) -> torch.Tensor:
+        self.gen.manual_seed(self.seed * 1_000_003 + self._index(name))
+        w = torch.randn(shape, generator=self.gen, device=self.device, dtype=torch.float32)
+        return (w * 0.02).to(torch.float16)
+
+    def packed(self, name: str, shape) -> PackedWeight:
+        return quantize_tensor(self.tensor(name, shape), self.qcfg)
+
+
+class PackedModel:
+    """Full (unsharded) packed weights of a decoder held in memory: the
+    layers' linears as ``layers.<i>.<q|k|v|o|gate|up|down>``, the LM head as
+    ``lm_head`` (packed or fp16) and the fp16 embedding as ``embed``."""
+
+    def __init__(self, cfg: DecoderConfig, qcfg: QuantConfig, packed: dict, tensors: dict):
+        self.cfg, self.qcfg, self.packed_weights, self.tensors = cfg, qcfg, packed, tensors
+
+    def packed(self, name: str, shape) -> PackedWeight:
+        pw = self.packed_weights[name]
+        if tuple(pw.shape) != tuple(shape) or pw.config != self.qcfg:
+            raise ValueError(f"{name}: stored {pw.shape} {pw.config}, expected {tuple(shape)} "
+                             f"{self.qcfg}")
+        return pw
+
+    def tensor(self, name: str, shape) -> torch.Tensor:
+        t = self.tensors[name]
+        if tuple(t.shape) != tuple(shape):
+            raise ValueError(f"{name}: stored {list(t.shape)}, expected {list(shape)}")
+        return t
+
+    @classmethod
+    def build(cls, cfg: DecoderConfig, qcfg: QuantConfig, seed: int = 0, device=None,
+              quantize_lm_head: bool = True) -> "PackedModel":
+        """The weights ``TPDecoder`` draws from ``seed``, packed once."""
+        src = SeededWeights(qcfg, seed, torch.device(device or "cpu"))
+        packed, tensors = {}, {"embed": src.tensor("embed", (cfg.vocab, cfg.hidden))}
+        for layer in range(cfg.n_layers):
+            for mat, shape in layer_shapes(cfg).items():
+                packed[f"layers.{layer}.{mat}"] = src.packed(f"layers.{layer}.{mat}", shape)
+        head = src.tensor("lm_head", (cfg.vocab, cfg.hidden))
+        if quantize_lm_head:
+            packed["lm_head"] = quantize_tensor(head, qcfg)
+        else:
+            tensors["lm_head"] = head
+        return cls(cfg, qcfg, packed, tensors)
+
+    def save(self, path) -> None:
+        """Write to ``path`` in the ``packed_io`` format."""
+        from dataclasses import asdict
+
+        from dequant_project_b200.packed_io import save_packed
+        q = self.qcfg
+        save_packed(path, self.packed_weights, self.tensors,
+                    meta={"decoder": asdict(self.cfg),
+                          "quant": {"bits": q.bits, "group_size": q.group_size,
+                                    "symmetric": q.symmetric, "layout": q.layout}})
+
+    @classmethod
+    def load(cls, path, device=None) -> "PackedModel":
+        """Read a file written by ``save`` (tensors moved to ``device``)."""
+        from dequant_project_b200.packed_io import load_packed
+        packed, tensors, meta = load_packed(path, device)
+        try:
+            cfg = DecoderConfig(**meta["decoder"])
+            qcfg = QuantConfig(**meta["quant"])
+        except (KeyError, TypeError) as exc:
+            raise ValueError(f"{path}: no decoder metadata ({exc})") from None
+        return cls(cfg, qcfg, packed, tensors)
+
+
 class TPDecoder:
     """This rank's shard of a packed decoder, plus its KV cache.
 
@@ -117,12 +219,16 @@ class TPDecoder:
     dimension splits on quantization-group boundaries
     (``intermediate_bounds``), the vocabulary evenly to within one row.
     ``linear_fn(x, pw)`` replaces the GEMV (tests run the host logic on the
-    CPU with a dequantize-then-matmul stand-in)."""
+    CPU with a dequantize-then-matmul stand-in). ``weights`` is where the full
+    matrices come from: ``None`` draws them from ``seed`` and quantizes them
+    (``SeededWeights``); a ``PackedModel`` (``PackedModel.load`` reads one
+    from disk) supplies them already packed, so no rank quantizes anything.
+    Each rank takes its shard of every full matrix."""
 
     def __init__(self, cfg: DecoderConfig, qcfg: QuantConfig, *, world: int = 1, rank: int = 0,
                  group=None, device=None, seed: int = 0, batch: int = 1, kv_len: int = 2048,
                  max_new: int = 1, quantize_lm_head: bool = True,
-                 linear_fn: Callable | None = None):
+                 linear_fn: Callable | None = None, weights=None):
         if cfg.n_heads % world or cfg.n_kv_heads % world:
             raise ValueError(f"{cfg.n_heads} query / {cfg.n_kv_heads} KV heads do not split "
                              f"over {world} ranks")
@@ -137,15 +243,20 @@ class TPDecoder:
         d = cfg.head_dim
         self.hq = cfg.n_heads // world
         self.hkv = cfg.n_kv_heads // world
-        gen = torch.Generator(device=self.device)
+        src = weights if weights is not None else SeededWeights(qcfg, seed, self.device)
+        if isinstance(src, PackedModel):
+            if src.cfg != cfg or src.qcfg != qcfg:
+                raise ValueError("the packed model's configuration differs from cfg/qcfg")
+            quantize_lm_head = "lm_head" in src.packed_weights
+        shapes = layer_shapes(cfg)
 
-        def weight(shape, idx):
-            gen.manual_seed(seed * 1_000_003 + idx)
-            w = torch.randn(shape, generator=gen, device=self.device, dtype=torch.float32)
-            return (w * 0.02).to(torch.float16)
-
-        def packed(shape, idx):
-            return quantize_tensor(weight(shape, idx), qcfg)
+        def packed(layer, mat):
+            pw = src.packed(f"layers.{layer}.{mat}", shapes[mat])
+            if pw.qweight.device != self.device:
+                pw = PackedWeight(pw.qweight.to(self.device), pw.scales.to(self.device),
+                                  None if pw.zeros is None else pw.zeros.to(self.device),
+                                  pw.config, pw.shape)
+            return pw
 
         q_bounds = [b * self.hq * d for b in range(world + 1)]
         kv_bounds = [b * self.hkv * d for b in range(world + 1)]
@@ -153,35 +264,38 @@ class TPDecoder:
         self.vocab_bounds = split_bounds(cfg.vocab, world)
         self.layers = []
         for layer in range(cfg.n_layers):
-            base = 16 * (layer + 1)
-            wq = packed((cfg.n_heads * d, cfg.hidden), base + 0)
-            wk = packed((cfg.n_kv_heads * d, cfg.hidden), base + 1)
-            wv = packed((cfg.n_kv_heads * d, cfg.hidden), base + 2)
+            wq, wk, wv = packed(layer, "q"), packed(layer, "k"), packed(layer, "v")
             qkv = cat_rows([shard_columns(wq, world, rank, q_bounds),
                             shard_columns(wk, world, rank, kv_bounds),
                             shard_columns(wv, world, rank, kv_bounds)])
             del wq, wk, wv
-            wo = packed((cfg.hidden, cfg.n_heads * d), base + 3)
+            wo = packed(layer, "o")
             o, _, _ = shard_rows(wo, world, rank, q_bounds)
             del wo
-            wg = packed((cfg.intermediate, cfg.hidden), base + 4)
-            wu = packed((cfg.intermediate, cfg.hidden), base + 5)
+            wg, wu = packed(layer, "gate"), packed(layer, "up")
             gu = cat_rows([shard_columns(wg, world, rank, self.inter_bounds),
                            shard_columns(wu, world, rank, self.inter_bounds)])
             del wg, wu
-            wd = packed((cfg.hidden, cfg.intermediate), base + 6)
+            wd = packed(layer, "down")
             down, _, _ = shard_rows(wd, world, rank, self.inter_bounds)
             del wd
             self.layers.append({"qkv": qkv, "o": o, "gu": gu, "down": down})
         self.ir = self.inter_bounds[rank + 1] - self.inter_bounds[rank]
-        self.embed = weight((cfg.vocab, cfg.hidden), 1)
-        head = weight((cfg.vocab, cfg.hidden), 2)
+        self.embed = src.tensor("embed", (cfg.vocab, cfg.hidden)).to(self.device)
         lo, hi = self.vocab_bounds[rank], self.vocab_bounds[rank + 1]
-        if quantize_lm_head:
-            self.lm_head = shard_columns(quantize_tensor(head, qcfg), world, rank,
-                                         self.vocab_bounds)
+        if isinstance(src, PackedModel) and quantize_lm_head:
+            head = src.packed("lm_head", (cfg.vocab, cfg.hidden))
+            head = PackedWeight(head.qweight.to(self.device), head.scales.to(self.device),
+                                None if head.zeros is None else head.zeros.to(self.device),
+                                head.config, head.shape)
+            self.lm_head = shard_columns(head, world, rank, self.vocab_bounds)
         else:
-            self.lm_head = head[lo:hi].contiguous()
+            head = src.tensor("lm_head", (cfg.vocab, cfg.hidden)).to(self.device)
+            if quantize_lm_head:
+                self.lm_head = shard_columns(quantize_tensor(head, qcfg), world, rank,
+                                             self.vocab_bounds)
+            else:
+                self.lm_head = head[lo:hi].contiguous()
         del head
         ones = torch.ones(cfg.hidden, dtype=torch.float16, device=self.device)
         self.attn_norm = [ones] * cfg.n_layers
