@@ -18,6 +18,11 @@ scaling, no collective on the data path). ``e2e`` is the same metric through
 the public ``dequant_cuda.gemv`` call with the activations copied from pinned
 host memory and the outputs copied back inside the timed region.
 
+``decode`` adds decode ms/token of the tensor-parallel decoder at TP = N
+(Llama-2-7B architecture, every linear and the LM head INT4
+g128 packed, batch 1, 2048-token fp16 KV cache), from a CUDA graph of one step,
+max over ranks (dequant_project_b200/decode_bench.py).
+
 ``--impl reference`` times the reference's CPU path (the C restatement of
 ``F.linear(x, packer.dequantize(pw))`` in oracle/, all host threads) on a
 bounded row sample of the same 18 cases, on rank 0 only.
@@ -230,6 +235,18 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(cs, data, budget_s=args.cpu_seconds)
 
+    # Decode ms/token of the tensor-parallel decoder at TP = world (BASELINE
+    # config 4: Llama-2-7B architecture, INT4 g128, batch 1, 2048-token KV
+    # cache), timed the same way (CUDA events, max over ranks). A failure here
+    # is reported in the line and never voids the GEMV result.
+    decode = None
+    if not args.no_decode:
+        try:
+            from dequant_project_b200 import decode_bench
+            decode = decode_bench.measure(decode_bench.default_args(), dist, rank, world, dev)
+        except Exception as exc:  # noqa: BLE001
+            decode = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
     traffic = load_traffic()
     if rank == 0:
         line = {
@@ -254,6 +271,7 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks,
             "cpu_baseline": cpu,
             "detail": detail,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     del graph
@@ -472,6 +490,8 @@ def main():
     ap.add_argument("--no-detail", action="store_true", help="skip the per-case table")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the decoder ms/token measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

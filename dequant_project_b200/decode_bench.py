@@ -29,20 +29,16 @@ import torch
 MODELS = {"llama2-7b": "LLAMA2_7B", "llama3-70b": "LLAMA3_70B"}
 
 
-def run(args) -> dict | None:
+def measure(args, dist, rank: int, world: int, dev: torch.device) -> dict | None:
+    """Build this rank's shard, capture and time the step (see the module
+    text) inside an existing process group (``dist`` is None for one GPU).
+    Every rank takes the same collective steps; rank 0 returns the result
+    line, the others None."""
     from dequant_project_b200 import decoder as D
     from dequant_project_b200.byte_model import measured_peaks
     from dequant_project_b200.packer import QuantConfig
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    local = dev.index
     cfg = getattr(D, MODELS[args.model])
     if args.layers:
         cfg = D.DecoderConfig(args.layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads,
@@ -74,31 +70,56 @@ def run(args) -> dict | None:
         dist.barrier(device_ids=[local])
     by = dec.step_bytes(args.kv_len)
     gr.release()
+    del gr, dec
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
     peaks = measured_peaks()
-    line = None
-    if rank == 0:
-        gbs = by["total"] / (ms * 1e-3) / 1e9
-        line = {
-            "metric": "decode ms/token", "value": round(ms, 4), "unit": "ms/token",
-            "tokens_per_s": round(args.batch / (ms * 1e-3), 1), "n_gpus": world,
-            "tp": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": False,
-            "config": {"model": args.model, "layers": cfg.n_layers, "batch": args.batch,
-                       "kv_len": args.kv_len, "bits": args.bits,
-                       "group_size": args.group_size or "per-channel",
-                       "symmetric": args.sym, "lm_head": "packed, column-parallel"},
-            "data": "synthetic (random-init N(0,0.02) weights, N(0,1) fp16 KV cache)",
-            "bytes_per_rank": by,
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
-                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
-                         "floor_ms": round(by["total"] / (peaks["hbm_gbs"] * 1e9) * 1e3, 4)},
-        }
-    if dist is not None:
-        dist.destroy_process_group()
-    return line
+    gbs = by["total"] / (ms * 1e-3) / 1e9
+    return {
+        "metric": "decode ms/token", "value": round(ms, 4), "unit": "ms/token",
+        "tokens_per_s": round(args.batch / (ms * 1e-3), 1), "n_gpus": world,
+        "tp": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": False,
+        "config": {"model": args.model, "layers": cfg.n_layers, "batch": args.batch,
+                   "kv_len": args.kv_len, "bits": args.bits,
+                   "group_size": args.group_size or "per-channel",
+                   "symmetric": args.sym, "lm_head": "packed, column-parallel"},
+        "data": "synthetic (random-init N(0,0.02) weights, N(0,1) fp16 KV cache)",
+        "bytes_per_rank": by,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "floor_ms": round(by["total"] / (peaks["hbm_gbs"] * 1e9) * 1e3, 4)},
+    }
 
 
-def main() -> None:
+def run(args) -> dict | None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    try:
+        return measure(args, dist, rank, world, dev)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+def default_args(**kw) -> argparse.Namespace:
+    """The CLI's defaults (Llama-2-7B, INT4 g128 asym, batch 1, 2048-token
+    cache), overridden by ``kw``."""
+    ns = _parser().parse_args([])
+    for k, v in kw.items():
+        setattr(ns, k, v)
+    return ns
+
+
+def _parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--model", choices=sorted(MODELS), default="llama2-7b")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count")
@@ -110,8 +131,11 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
-    args = ap.parse_args()
-    line = run(args)
+    return ap
+
+
+def main() -> None:
+    line = run(_parser().parse_args())
     if line is not None:
         print(json.dumps(line), flush=True)
 
