@@ -2,7 +2,10 @@
 
 Run once, in a container where the reference project is mounted:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [REFERENCE_ROOT]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py REFERENCE_ROOT
+
+(REFERENCE_ROOT, or the environment variable DEQUANT_REFERENCE_ROOT: the
+checkout of the reference project.)
 
 It imports the reference's own packer (``dequant/packer.py`` of
 KrishnaI2424/Dequant_Project, read-only) and its CPU GEMV path
@@ -109,4 +112,8 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import os
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DEQUANT_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (the reference project's checkout)")
+    main(root)
