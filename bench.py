@@ -18,6 +18,10 @@ scaling, no collective on the data path). ``e2e`` is the same metric through
 the public ``dequant_cuda.gemv`` call with the activations copied from pinned
 host memory and the outputs copied back inside the timed region.
 
+``shape_sweep`` (one GPU) is BASELINE config 3: INT4 g128 at batch 1 over
+(4096,4096), (12288,4096), (4096,14336), (28672,8192), (8192,28672) and
+(128256,4096), per case µs and GB/s.
+
 ``decode`` adds decode ms/token of the tensor-parallel decoder at TP = N
 (Llama-2-7B architecture, every linear and the LM head INT4
 g128 packed, batch 1, 2048-token fp16 KV cache), from a CUDA graph of one step,
@@ -226,6 +230,12 @@ def run_ours(args, rank, world, local_rank):
     detail = None
     if rank == 0 and world == 1 and not args.no_detail:
         detail = per_case_detail(dev, cs, data, peaks)
+    shapes = None
+    if rank == 0 and world == 1 and not args.no_detail:
+        try:
+            shapes = shape_sweep(dev, peaks)
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
+            shapes = {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
     # End to end through the public API with host buffers.
     e2e = run_e2e(dev, cs, data, args, dist, local_rank)
@@ -272,6 +282,7 @@ def run_ours(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "detail": detail,
             "decode": decode,
+            "shape_sweep": shapes,
         }
         print(json.dumps(line), flush=True)
     del graph
@@ -280,7 +291,34 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def per_case_detail(dev, cs, data, peaks, reps=20):
+SHAPE_SWEEP = [(4096, 4096), (12288, 4096), (4096, 14336), (28672, 8192), (8192, 28672),
+               (128256, 4096)]
+
+
+def shape_sweep(dev, peaks):
+    """INT4 g128 asymmetric at batch 1 over the six shapes,
+    per-case µs and GB/s measured like ``per_case_detail`` (distinct weight
+    copies replayed from one graph, more bytes than L2 per replay)."""
+    import torch
+
+    from dequant_project_b200.packer import QuantConfig, quantize_tensor
+
+    cs, data = [], []
+    for i, (n, k) in enumerate(SHAPE_SWEEP):
+        g = torch.Generator(device=dev).manual_seed(7000 + i)
+        w = torch.randn(n, k, dtype=torch.float16, device=dev, generator=g) * 0.02
+        pw = quantize_tensor(w, QuantConfig(4, 128, False))
+        del w
+        x = torch.randn(1, k, dtype=torch.float16, device=dev, generator=g)
+        cs.append((n, k, 4, 128, False, 1, "int4-g128-asym"))
+        data.append((pw, x))
+    rows = per_case_detail(dev, cs, data, peaks, min_copies=4)
+    del data
+    torch.cuda.empty_cache()
+    return rows
+
+
+def per_case_detail(dev, cs, data, peaks, reps=20, min_copies=28):
     import torch
 
     from dequant_project_b200 import dequant_cuda
@@ -289,7 +327,7 @@ def per_case_detail(dev, cs, data, peaks, reps=20):
     rows = []
     for (n, k, bits, gs, sym, m, name), (pw, x) in zip(cs, data):
         b = case_bytes(n, k, bits, gs, sym, m)
-        copies = max(28, math.ceil(8 * l2 / pw.nbytes))
+        copies = max(min_copies, math.ceil(8 * l2 / pw.nbytes))
         ws = [(pw.qweight.clone(), pw.scales.clone(),
                None if pw.zeros is None else pw.zeros.clone()) for _ in range(copies)]
 
