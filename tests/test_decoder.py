@@ -150,3 +150,25 @@ def test_gloo_two_ranks_match_one_rank():
     ref = one.step(torch.tensor([5, 977]), one.kv_len).float()
     err = (out[0][1].float() - ref).abs().max() / ref.abs().max()
     assert err < 5e-3, err
+
+
+def test_step_bytes_follow_the_reference_decode_model():
+    """Per-rank bytes of a step: the packed weights are exactly the reference
+    byte model's quantized bytes (numel * bits / 8 + one fp16 scale and zero
+    per group, dequant/byte_model.py:165-176) for the layers and the LM head,
+    split without overlap across ranks; the KV term reads positions 0..pos and
+    writes one slot."""
+    cfg, q = TINY, QCFG
+    d = cfg.head_dim
+    quantizable = cfg.n_layers * (cfg.hidden * (cfg.n_heads + 2 * cfg.n_kv_heads) * d
+                                  + cfg.hidden * cfg.n_heads * d
+                                  + 3 * cfg.hidden * cfg.intermediate) + cfg.vocab * cfg.hidden
+    expect = quantizable * q.bits // 8 + quantizable // q.group_size * 2 * 2
+    one = TPDecoder(cfg, q, batch=2, kv_len=24, linear_fn=cpu_linear)
+    by = one.step_bytes(24)
+    assert by["weights"] == expect
+    assert by["kv_cache"] == cfg.n_layers * 2 * 2 * cfg.n_kv_heads * d * 2 * (25 + 1)
+    ranks = [TPDecoder(cfg, q, world=2, rank=r, batch=2, kv_len=24, linear_fn=cpu_linear)
+             for r in range(2)]
+    assert sum(r.step_bytes(24)["weights"] for r in ranks) == expect
+    assert sum(r.step_bytes(24)["kv_cache"] for r in ranks) == by["kv_cache"]
