@@ -45,13 +45,16 @@ def lib() -> ctypes.CDLL:
     h.dqg_rope_kv_append.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
     h.dqg_silu_mul.restype = i32
     h.dqg_silu_mul.argtypes = [vp, vp, i64, i64, vp]
+    h.dqg_stream_plan.restype = i32
+    h.dqg_stream_plan.argtypes = [i64, i64, i64, i64, i64, i32, ctypes.POINTER(ctypes.c_int32), i32]
     _lib = h
     return _lib
 
 
 # Every symbol the C header declares; tests check the library exports them all.
 EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_dequantize",
-            "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul")
+            "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul",
+            "dqg_stream_plan")
 
 
 def check(rc: int) -> None:

@@ -311,6 +311,26 @@ int dqg_silu_mul(const void* gate_up, void* out, int64_t M, int64_t I, void* str
   return ok();
 }
 
+int dqg_stream_plan(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+                    int num_sms, int32_t* out, int out_len) {
+  if (out == nullptr || out_len < 23) return fail(DQG_ERR_INVALID, "out needs 23 entries");
+  if (M < 1 || M > 8 || N < 1 || K < 1 || N > (1 << 30) || K > (1 << 30) || num_sms < 1)
+    return fail(DQG_ERR_INVALID, "shape out of range");
+  if (bits != 2 && bits != 4 && bits != 8) return fail(DQG_ERR_INVALID, "bits must be 2, 4 or 8");
+  if (group_size <= 0 || K % group_size)
+    return fail(DQG_ERR_INVALID, "K must be a multiple of group_size");
+  dqg::StreamPlan pl;
+  if (!dqg::plan_stream(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                        static_cast<int>(bits), static_cast<int>(group_size), num_sms, &pl))
+    return fail(DQG_ERR_UNSUPPORTED, "no streaming plan for this shape");
+  const int32_t v[23] = {pl.wpl, pl.mp, pl.ks, pl.n_slabs, pl.stages, pl.n_meta, pl.w_pitch,
+                         pl.xp, pl.stage_bytes, pl.C, pl.KC, pl.off_x, pl.off_sstep, pl.off_sx,
+                         pl.off_meta, pl.meta_half, pl.meta_stride, pl.off_red, pl.off_bar,
+                         pl.off_xred, pl.off_zero, pl.smem, pl.grid};
+  for (int i = 0; i < 23; ++i) out[i] = v[i];
+  return ok();
+}
+
 int dqg_device_status(int device, uint32_t* status, int reset) {
   if (status == nullptr) return fail(DQG_ERR_INVALID, "status must not be null");
   cudaError_t e = dqg::read_device_status(device, status, reset != 0);

@@ -89,6 +89,18 @@ int dqg_dequantize(const int32_t *qweight, const void *scales, const void *zeros
 int dqg_device_status(int device, uint32_t *status, int reset);
 
 /*
+ * The streaming GEMV kernel's launch plan for a shape (host arithmetic only,
+ * no device access): out[0..22] = wpl, mp, ks, n_slabs, stages, n_meta,
+ * w_pitch, xp, stage_bytes, C (cluster size), KC (codes per cluster rank),
+ * off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar,
+ * off_xred, off_zero, smem (bytes), grid. Returns DQG_ERR_UNSUPPORTED when the
+ * shape takes the fallback kernel. For tests and diagnostics; no reference
+ * counterpart.
+ */
+int dqg_stream_plan(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+                    int num_sms, int32_t *out, int out_len);
+
+/*
  * Element-wise steps of the tensor-parallel decoder around the GEMVs
  * (dequant_project_b200/decoder.py). No reference counterpart: the reference
  * only models the decode step as bytes (dequant/byte_model.py:179-251). fp16
