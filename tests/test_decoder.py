@@ -120,13 +120,15 @@ def test_rejects_head_counts_that_do_not_split():
         TPDecoder(TINY, QCFG, world=3, linear_fn=cpu_linear)
 
 
-def test_gloo_two_ranks_match_one_rank():
+@pytest.mark.parametrize("fmt", [(4, 64, False), (8, None, True), (2, 64, False)],
+                         ids=("int4-g64", "int8-perchannel", "int2-g64"))
+def test_gloo_two_ranks_match_one_rank(fmt):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
     import tp_workers
-    procs = [ctx.Process(target=tp_workers.decoder_step, args=(r, world, port, q))
+    procs = [ctx.Process(target=tp_workers.decoder_step, args=(r, world, port, q, fmt))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -146,7 +148,7 @@ def test_gloo_two_ranks_match_one_rank():
     for r, (status, val) in out.items():
         assert status == "ok", val
     assert torch.equal(out[0][1], out[1][1])
-    one = TPDecoder(TINY, QCFG, seed=3, batch=2, kv_len=24, linear_fn=cpu_linear)
+    one = TPDecoder(TINY, QuantConfig(*fmt), seed=3, batch=2, kv_len=24, linear_fn=cpu_linear)
     ref = one.step(torch.tensor([5, 977]), one.kv_len).float()
     err = (out[0][1].float() - ref).abs().max() / ref.abs().max()
     assert err < 5e-3, err

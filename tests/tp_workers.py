@@ -82,7 +82,7 @@ def tp_rank_fails(rank, world, port, queue):
         queue.put((rank, "error", f"{type(exc).__name__}: {exc}", None))
 
 
-def decoder_step(rank, world, port, queue):
+def decoder_step(rank, world, port, queue, fmt=(4, 64, False)):
     """One decode step of the tiny test decoder on this gloo rank."""
     try:
         from dequant_project_b200.decoder import DecoderConfig, TPDecoder
@@ -90,7 +90,7 @@ def decoder_step(rank, world, port, queue):
         dist = _init(rank, world, port, "gloo", 60)
         cfg = DecoderConfig(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640,
                             vocab=1000)
-        dec = TPDecoder(cfg, QuantConfig(4, 64, False), world=world, rank=rank, seed=3, batch=2,
+        dec = TPDecoder(cfg, QuantConfig(*fmt), world=world, rank=rank, seed=3, batch=2,
                         kv_len=24, linear_fn=_cpu_linear)
         out = dec.step(torch.tensor([5, 977]), dec.kv_len)
         queue.put((rank, "ok", out))
