@@ -174,3 +174,30 @@ def test_step_bytes_follow_the_reference_decode_model():
              for r in range(2)]
     assert sum(r.step_bytes(24)["weights"] for r in ranks) == expect
     assert sum(r.step_bytes(24)["kv_cache"] for r in ranks) == by["kv_cache"]
+
+
+def test_rank_failure_ends_the_step_with_an_error_not_a_hang():
+    import tp_workers
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=tp_workers.decoder_rank_fails, args=(r, 2, port, q))
+             for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    out = {}
+    while len(out) < 2 and time.time() - t0 < 120:
+        try:
+            r, status, val = q.get(timeout=1)
+            out[r] = (status, val)
+        except Exception:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert out.get(1, ("missing",))[0] == "error"
+    assert out.get(0, ("missing",))[0] == "error", out.get(0)
+    assert time.time() - t0 < 120

@@ -127,3 +127,22 @@ def decoder_step_nccl(rank, world, port, queue):
         dist.destroy_process_group()
     except Exception:
         queue.put((rank, "error", traceback.format_exc()))
+
+
+def decoder_rank_fails(rank, world, port, queue):
+    """Rank 1 raises before its first decode step; rank 0's step must end with
+    an error from its first collective (peer gone or timeout), not hang."""
+    try:
+        from dequant_project_b200.decoder import DecoderConfig, TPDecoder
+        from dequant_project_b200.packer import QuantConfig
+        _init(rank, world, port, "gloo", 5)
+        cfg = DecoderConfig(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640,
+                            vocab=1000)
+        dec = TPDecoder(cfg, QuantConfig(4, 64, False), world=world, rank=rank, seed=3,
+                        batch=1, kv_len=8, linear_fn=_cpu_linear)
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1 before the decode step")
+        dec.step(torch.tensor([5]), 8)
+        queue.put((rank, "completed", None))
+    except Exception as exc:
+        queue.put((rank, "error", f"{type(exc).__name__}: {exc}"))
