@@ -377,6 +377,22 @@ class TPDecoder:
         return torch.cat([p[:, :b - a] for p, a, b in
                           zip(parts, self.vocab_bounds[:-1], self.vocab_bounds[1:])], dim=1)
 
+    def generate(self, tokens: torch.Tensor, steps: int, start: int | None = None) -> torch.Tensor:
+        """Greedy decode: feed ``tokens`` [batch] at position ``start`` (default
+        ``kv_len``), then each step's argmax, ``steps`` times. Returns the
+        generated ids [batch, steps] (identical on every rank: the logits are
+        all-gathered before the argmax). Needs ``start + steps <= capacity``."""
+        pos = self.kv_len if start is None else start
+        if pos + steps > self.capacity:
+            raise ValueError(f"{steps} steps from position {pos} exceed the cache capacity "
+                             f"{self.capacity}")
+        out = []
+        cur = tokens
+        for t in range(steps):
+            cur = self.step(cur, pos + t).argmax(dim=-1)
+            out.append(cur)
+        return torch.stack(out, dim=1)
+
     def packed_bytes(self) -> int:
         """Bytes of this rank's packed weights (layers and LM head)."""
         n = sum(pw.nbytes for w in self.layers for pw in w.values())

@@ -201,3 +201,17 @@ def test_rank_failure_ends_the_step_with_an_error_not_a_hang():
     assert out.get(1, ("missing",))[0] == "error"
     assert out.get(0, ("missing",))[0] == "error", out.get(0)
     assert time.time() - t0 < 120
+
+
+def test_generate_is_greedy_stepping():
+    dec = TPDecoder(TINY, QCFG, seed=2, batch=2, kv_len=10, max_new=4, linear_fn=cpu_linear)
+    ids = dec.generate(torch.tensor([3, 400]), 4)
+    assert ids.shape == (2, 4) and ids.dtype == torch.int64
+    dec.reset_cache(2)                      # same cache contents again
+    cur, want = torch.tensor([3, 400]), []
+    for t in range(4):
+        cur = dec.step(cur, 10 + t).argmax(dim=-1)
+        want.append(cur)
+    assert torch.equal(ids, torch.stack(want, dim=1))
+    with pytest.raises(ValueError, match="exceed the cache"):
+        dec.generate(torch.tensor([3, 400]), 5)
