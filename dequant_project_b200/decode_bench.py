@@ -4,6 +4,8 @@
         [--group-size 128] [--batch 1] [--kv-len 2048] [--steps 50] [--warmup 5]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
         -m dequant_project_b200.decode_bench ...
+    python -m dequant_project_b200.decode_bench --model llama3-70b --save-weights m.pt
+    python -m dequant_project_b200.decode_bench --weights m.pt     # no quantization
 
 One process per GPU; the tensor-parallel width is the world size. The model
 (random N(0, 0.02) weights, every linear packed, N(0, 1) fp16 KV cache of
@@ -36,16 +38,12 @@ def measure(args, dist, rank: int, world: int, dev: torch.device) -> dict | None
     line, the others None."""
     from dequant_project_b200 import decoder as D
     from dequant_project_b200.byte_model import measured_peaks
-    from dequant_project_b200.packer import QuantConfig
 
     local = dev.index
-    cfg = getattr(D, MODELS[args.model])
-    if args.layers:
-        cfg = D.DecoderConfig(args.layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads,
-                              cfg.intermediate, cfg.vocab, cfg.rope_theta, cfg.eps)
-    q = QuantConfig(args.bits, args.group_size or None, args.sym)
+    cfg, q, weights = model_source(args, dev)
     dec = D.TPDecoder(cfg, q, world=world, rank=rank, device=dev, seed=args.seed,
-                      batch=args.batch, kv_len=args.kv_len)
+                      batch=args.batch, kv_len=args.kv_len, weights=weights)
+    del weights
     torch.cuda.synchronize(dev)
     gr = D.DecodeGraph(dec, args.kv_len)
     stream = torch.cuda.current_stream(dev)
@@ -81,16 +79,43 @@ def measure(args, dist, rank: int, world: int, dev: torch.device) -> dict | None
         "tokens_per_s": round(args.batch / (ms * 1e-3), 1), "n_gpus": world,
         "tp": world, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": False,
-        "config": {"model": args.model, "layers": cfg.n_layers, "batch": args.batch,
-                   "kv_len": args.kv_len, "bits": args.bits,
-                   "group_size": args.group_size or "per-channel",
-                   "symmetric": args.sym, "lm_head": "packed, column-parallel"},
+        "config": {"model": args.model if not getattr(args, "weights", None) else args.weights,
+                   "layers": cfg.n_layers, "batch": args.batch,
+                   "kv_len": args.kv_len, "bits": q.bits,
+                   "group_size": q.group_size or "per-channel",
+                   "symmetric": q.symmetric, "lm_head": "packed, column-parallel"},
         "data": "synthetic (random-init N(0,0.02) weights, N(0,1) fp16 KV cache)",
         "bytes_per_rank": by,
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
                      "floor_ms": round(by["total"] / (peaks["hbm_gbs"] * 1e9) * 1e3, 4)},
     }
+
+
+def model_source(args, device):
+    """(DecoderConfig, QuantConfig, weights): the packed file ``args.weights``
+    when given (its configuration wins), else the named model drawn from
+    ``args.seed``."""
+    from dequant_project_b200 import decoder as D
+    from dequant_project_b200.packer import QuantConfig
+
+    if getattr(args, "weights", None):
+        model = D.PackedModel.load(args.weights, device=device)
+        return model.cfg, model.qcfg, model
+    cfg = getattr(D, MODELS[args.model])
+    if args.layers:
+        cfg = D.DecoderConfig(args.layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads,
+                              cfg.intermediate, cfg.vocab, cfg.rope_theta, cfg.eps)
+    return cfg, QuantConfig(args.bits, args.group_size or None, args.sym), None
+
+
+def save_model(args, device) -> None:
+    """Pack the named model once (on ``device``) and write it to
+    ``args.save_weights``, for later runs with ``--weights``."""
+    from dequant_project_b200 import decoder as D
+
+    cfg, q, _ = model_source(argparse.Namespace(**{**vars(args), "weights": None}), device)
+    D.PackedModel.build(cfg, q, seed=args.seed, device=device).save(args.save_weights)
 
 
 def run(args) -> dict | None:
@@ -131,11 +156,19 @@ def _parser() -> argparse.ArgumentParser:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--weights", default=None,
+                    help="load the packed model from this file (packed_io format)")
+    ap.add_argument("--save-weights", default=None,
+                    help="pack the model once, write it to this file and exit")
     return ap
 
 
 def main() -> None:
-    line = run(_parser().parse_args())
+    args = _parser().parse_args()
+    if args.save_weights:
+        save_model(args, torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+        return
+    line = run(args)
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -63,3 +63,18 @@ def test_decoder_from_file_matches_seeded_decoder(tmp_path, quantize_head):
     assert torch.equal(a.step(tok, 16), b.step(tok, 16))
     with pytest.raises(ValueError, match="differs"):
         TPDecoder(cfg, QuantConfig(2, 64, False), weights=loaded, linear_fn=cpu_linear)
+
+
+def test_decode_bench_loads_a_saved_model(tmp_path):
+    """decode_bench's --save-weights / --weights source (CPU tensors here)."""
+    from dequant_project_b200 import decode_bench
+    cfg = DecoderConfig(n_layers=1, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640,
+                        vocab=500)
+    q = QuantConfig(2, 64, False)
+    PackedModel.build(cfg, q, seed=4).save(tmp_path / "m.pt")
+    got_cfg, got_q, model = decode_bench.model_source(
+        decode_bench.default_args(weights=str(tmp_path / "m.pt")), torch.device("cpu"))
+    assert got_cfg == cfg and got_q == q and isinstance(model, PackedModel)
+    cfg7, q7, none = decode_bench.model_source(decode_bench.default_args(layers=2),
+                                               torch.device("cpu"))
+    assert none is None and cfg7.n_layers == 2 and cfg7.hidden == 4096 and q7.bits == 4
