@@ -45,6 +45,11 @@ def lib() -> ctypes.CDLL:
     h.dqg_rope_kv_append.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
     h.dqg_silu_mul.restype = i32
     h.dqg_silu_mul.argtypes = [vp, vp, i64, i64, vp]
+    h.dqg_set_weight_prefetch.restype = i32
+    h.dqg_set_weight_prefetch.argtypes = [i32]
+    h.dqg_debug_gemv_starved.restype = i32
+    h.dqg_debug_gemv_starved.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32,
+                                         ctypes.c_uint64, vp]
     h.dqg_stream_plan.restype = i32
     h.dqg_stream_plan.argtypes = [i64, i64, i64, i64, i64, i32, ctypes.POINTER(ctypes.c_int32), i32]
     _lib = h
@@ -54,7 +59,7 @@ def lib() -> ctypes.CDLL:
 # Every symbol the C header declares; tests check the library exports them all.
 EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_dequantize",
             "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul",
-            "dqg_stream_plan")
+            "dqg_stream_plan", "dqg_set_weight_prefetch", "dqg_debug_gemv_starved")
 
 
 def check(rc: int) -> None:

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <cuda_runtime.h>
 
@@ -48,6 +49,45 @@ int check_device_ptr(const void* p, int dev, const char* name) {
   if (attr.type == cudaMemoryTypeDevice && attr.device != dev)
     return fail(DQG_ERR_INVALID, "%s and qweight must be on the same device", name);
   return DQG_OK;
+}
+
+// Pointer-kind checks (cudaPointerGetAttributes on every operand) cost a few
+// microseconds per call, which is comparable to a small GEMV; they run only
+// when DQG_CHECK_POINTERS is set to a non-empty value other than "0". The
+// Python binding checks tensor devices itself, and alignment and size checks
+// always run.
+bool pointer_checks() {
+  static const bool on = [] {
+    const char* v = std::getenv("DQG_CHECK_POINTERS");
+    return v != nullptr && v[0] != '\0' && std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
+
+// Streaming-kernel plans of recent call shapes (direct-mapped, per thread):
+// a decode step calls a handful of shapes over and over.
+struct PlanEntry {
+  int M, N, K, bits, group_size, sms;
+  bool ok;
+  dqg::StreamPlan plan;
+  bool used;
+};
+
+bool cached_stream_plan(int M, int N, int K, int bits, int group_size, int sms,
+                        dqg::StreamPlan* out) {
+  thread_local PlanEntry cache[32] = {};
+  const uint32_t h = (static_cast<uint32_t>(M) * 2654435761u) ^ (static_cast<uint32_t>(N) * 40503u) ^
+                     (static_cast<uint32_t>(K) * 2246822519u) ^ static_cast<uint32_t>(bits << 3) ^
+                     static_cast<uint32_t>(group_size) * 3266489917u ^ static_cast<uint32_t>(sms);
+  PlanEntry& e = cache[(h ^ (h >> 15)) & 31];
+  if (!(e.used && e.M == M && e.N == N && e.K == K && e.bits == bits &&
+        e.group_size == group_size && e.sms == sms)) {
+    e.ok = dqg::plan_stream(M, N, K, bits, group_size, sms, &e.plan);
+    e.M = M; e.N = N; e.K = K; e.bits = bits; e.group_size = group_size; e.sms = sms;
+    e.used = true;
+  }
+  if (e.ok) *out = e.plan;
+  return e.ok;
 }
 
 int sm_count(int dev) {
@@ -156,12 +196,14 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  rc = check_weight_ptrs(qweight, scales, zeros, dev);
-  if (rc) return rc;
-  rc = check_device_ptr(x, dev, "x");
-  if (rc) return rc;
-  rc = check_device_ptr(y, dev, "y");
-  if (rc) return rc;
+  if (pointer_checks()) {
+    rc = check_weight_ptrs(qweight, scales, zeros, dev);
+    if (rc) return rc;
+    rc = check_device_ptr(x, dev, "x");
+    if (rc) return rc;
+    rc = check_device_ptr(y, dev, "y");
+    if (rc) return rc;
+  }
 
   dqg::GemvArgs a;
   a.x = static_cast<const uint16_t*>(x);
@@ -182,9 +224,9 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   const bool meta_aligned = reinterpret_cast<uintptr_t>(scales) % 16 == 0 &&
                             (zeros == nullptr || reinterpret_cast<uintptr_t>(zeros) % 16 == 0);
   if (meta_aligned &&
-      dqg::plan_stream(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-                       static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
-                       &splan)) {
+      cached_stream_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                         static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
+                         &splan)) {
     e = dqg::launch_stream(a, splan, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     return ok();
@@ -328,6 +370,55 @@ int dqg_stream_plan(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group
                          pl.off_meta, pl.meta_half, pl.meta_stride, pl.off_red, pl.off_bar,
                          pl.off_xred, pl.off_zero, pl.smem, pl.grid};
   for (int i = 0; i < 23; ++i) out[i] = v[i];
+  return ok();
+}
+
+int dqg_set_weight_prefetch(int enable) {
+  const int prev = dqg::weight_prefetch() ? 1 : 0;
+  dqg::set_weight_prefetch(enable != 0);
+  return prev;
+}
+
+int dqg_debug_gemv_starved(const int32_t* qweight, const void* scales, const void* zeros,
+                           void* y, const void* x, int64_t M, int64_t N, int64_t K, int64_t bits,
+                           int64_t group_size, int symmetric, int interleaved,
+                           uint64_t wait_ns, void* stream) {
+  if (wait_ns < 1000000ull || wait_ns > 1000000000ull)
+    return fail(DQG_ERR_INVALID, "wait_ns must be in [1 ms, 1 s], got %llu",
+                (unsigned long long)wait_ns);
+  if (M < 1 || M > dqg::kMaxM) return fail(DQG_ERR_INVALID, "M must be in [1, %d]", dqg::kMaxM);
+  int rc = check_weight_args(qweight, scales, zeros, N, K, bits, group_size, symmetric);
+  if (rc) return rc;
+  if (x == nullptr || y == nullptr) return fail(DQG_ERR_INVALID, "x and y must not be null");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(qweight) % 16 ||
+      reinterpret_cast<uintptr_t>(scales) % 16 ||
+      (zeros != nullptr && reinterpret_cast<uintptr_t>(zeros) % 16))
+    return fail(DQG_ERR_INVALID, "x, qweight, scales and zeros must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  dqg::StreamPlan splan;
+  if (!dqg::plan_stream(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                        static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
+                        &splan))
+    return fail(DQG_ERR_UNSUPPORTED, "no streaming plan for this shape");
+  if (splan.C != 1)
+    return fail(DQG_ERR_UNSUPPORTED, "the starved diagnostic runs single-CTA plans only");
+  dqg::GemvArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.qweight = reinterpret_cast<const uint32_t*>(qweight);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.zeros = static_cast<const uint16_t*>(zeros);
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.bits = static_cast<int>(bits);
+  a.group_size = static_cast<int>(group_size);
+  a.symmetric = symmetric != 0;
+  a.interleaved = interleaved != 0;
+  e = dqg::launch_stream(a, splan, static_cast<cudaStream_t>(stream), wait_ns, true);
+  if (e != cudaSuccess) return cuda_fail(e, "starved gemv launch");
   return ok();
 }
 

@@ -17,8 +17,9 @@ enum : uint32_t {
 };
 
 // One status word per translation unit that includes this header (internal
-// linkage; the library is built without relocatable device code). The unit
-// that launches waiting kernels also provides the host-side reader.
+// linkage; the library is built without relocatable device code). Every unit
+// whose kernels wait exports a reader of its own word (DQG_STATUS_READER
+// below), and the library's status query ORs all of them together.
 static __device__ uint32_t g_status = 0;
 
 // Upper bound on any single mbarrier wait (nanoseconds of %globaltimer). A
@@ -79,14 +80,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Bounded: after
-// kWaitLimitNs the wait gives up, flags kStatusWaitTimeout in g_status and
+// limit_ns the wait gives up, flags kStatusWaitTimeout in g_status and
 // returns false so that the caller can leave its loop and the kernel ends.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicOr(&g_status, kStatusWaitTimeout);
       return false;
     }
@@ -96,8 +98,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // mbar_wait taken by all 32 lanes of a warp with a warp-uniform outcome, so
 // that a timed-out warp leaves its loop as a whole (no lane is left behind in
 // a later __syncwarp or vote).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  const bool ok = mbar_wait(bar, parity);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  const bool ok = mbar_wait(bar, parity, limit_ns);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -115,6 +118,12 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
                ::: "memory");
+}
+
+// The same cluster barrier for threads that may arrive from different points
+// of their code (not converged within a warp).
+__device__ __forceinline__ void cluster_sync_all_unaligned() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // Address of the same shared-memory location in cluster CTA `rank`.
@@ -148,7 +157,8 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
-__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   bool ok = mbar_try_wait_cluster(bar, parity);
   if (!ok) {
     const uint64_t t0 = globaltimer();
@@ -157,7 +167,7 @@ __device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity
         ok = true;
         break;
       }
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicOr(&g_status, kStatusWaitTimeout);
         break;
       }
@@ -256,3 +266,17 @@ __device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t magic) {
 }
 
 }  // namespace dqg
+
+// Host-side reader of this translation unit's status word: defines
+// `cudaError_t NAME(uint32_t* status, bool reset)` (current device).
+#define DQG_STATUS_READER(NAME)                                                 \
+  namespace dqg {                                                               \
+  cudaError_t NAME(uint32_t* status, bool reset) {                              \
+    cudaError_t e = cudaMemcpyFromSymbol(status, g_status, sizeof(uint32_t));   \
+    if (e == cudaSuccess && reset) {                                            \
+      const uint32_t zero = 0;                                                  \
+      e = cudaMemcpyToSymbol(g_status, &zero, sizeof(uint32_t));                \
+    }                                                                           \
+    return e;                                                                   \
+  }                                                                             \
+  }

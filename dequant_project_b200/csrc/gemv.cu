@@ -634,10 +634,14 @@ cudaError_t read_device_status(int device, uint32_t* status, bool reset) {
   cudaError_t e = cudaGetDevice(&prev);
   if (e != cudaSuccess) return e;
   if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
-  e = cudaMemcpyFromSymbol(status, g_status, sizeof(uint32_t));
-  if (e == cudaSuccess && reset) {
-    const uint32_t zero = 0;
-    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(uint32_t));
+  cudaError_t (*readers[])(uint32_t*, bool) = {read_status_gemv, read_status_stream_b2,
+                                                read_status_stream_b4, read_status_stream_b8};
+  *status = 0;
+  for (auto rd : readers) {
+    uint32_t v = 0;
+    e = rd(&v, reset);
+    if (e != cudaSuccess) break;
+    *status |= v;
   }
   if (prev != device) cudaSetDevice(prev);
   return e;
@@ -790,3 +794,5 @@ cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& pl, cudaStream_t stre
 }
 
 }  // namespace dqg
+
+DQG_STATUS_READER(read_status_gemv)

@@ -76,7 +76,10 @@ cudaError_t launch_gemv(const GemvArgs& args, const GemvPlan& plan, cudaStream_t
 // codes unpacked to fp16 subnormals, no preparation warps. Used whenever its
 // plan fits; gemv_kernel above covers the rest (activations too large to keep
 // resident, or very many groups per row).
-constexpr int kStreamNCW = 8;     // consumer (tensor-core) warps
+#ifndef DQG_STREAM_NCW
+#define DQG_STREAM_NCW 8
+#endif
+constexpr int kStreamNCW = DQG_STREAM_NCW;  // consumer (tensor-core) warps
 constexpr int kStreamThreads = 32 * (2 + kStreamNCW);  // + producer + reducer
 constexpr int kStreamNRB = 4;     // tile reduction buffers
 constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations (per CTA)
@@ -99,6 +102,9 @@ struct StreamParams {
   int stage_bytes;
   int off_x, off_sstep, off_sx, off_meta, meta_half, meta_stride, off_red, off_bar, off_xred;
   int off_zero;           // zero block for non-live fragment columns
+  int prefetch;           // 1: the first weight ring is issued before the dependent-launch wait
+  int starve;             // diagnostic: 1 = the producer issues nothing (every wait gives up)
+  unsigned long long wait_ns;  // limit of each bounded wait
   long long tail_first;   // first scales/zeros element past the last 16-byte boundary
   int tail_n;             // number of such elements (0..7)
 };
@@ -111,7 +117,16 @@ struct StreamPlan {
 };
 
 bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, StreamPlan* plan);
-cudaError_t launch_stream(const GemvArgs& args, const StreamPlan& plan, cudaStream_t stream);
+
+// Process-wide switch (default on): the streaming kernel issues its first
+// weight ring before waiting for the previous grid on the stream.
+void set_weight_prefetch(bool on);
+bool weight_prefetch();
+// wait_ns: limit of each bounded wait in the kernel (0 = the default, 2 s);
+// starve: diagnostic launch whose producer issues no copies, so that every
+// wait of the kernel gives up after wait_ns and the status word records it.
+cudaError_t launch_stream(const GemvArgs& args, const StreamPlan& plan, cudaStream_t stream,
+                          unsigned long long wait_ns = 0, bool starve = false);
 
 struct DequantArgs {
   const uint32_t* qweight;
@@ -124,8 +139,13 @@ struct DequantArgs {
 
 cudaError_t launch_dequantize(const DequantArgs& args, cudaStream_t stream);
 
-// Read (and optionally clear) the device status word g_status of `device`.
+// Read (and optionally clear) the device status of `device`: the OR of the
+// status words of every translation unit whose kernels wait.
 cudaError_t read_device_status(int device, uint32_t* status, bool reset);
+cudaError_t read_status_gemv(uint32_t* status, bool reset);
+cudaError_t read_status_stream_b2(uint32_t* status, bool reset);
+cudaError_t read_status_stream_b4(uint32_t* status, bool reset);
+cudaError_t read_status_stream_b8(uint32_t* status, bool reset);
 
 cudaError_t launch_add_one(const float* x, float* out, int64_t n, cudaStream_t stream);
 

@@ -1,6 +1,7 @@
 // Host side of the streaming GEMV kernel (gemv_stream.cuh): shared-memory
 // plan and launch. The kernel variants are instantiated per bit width in
 // gemv_stream_b{2,4,8}.cu so that they compile in parallel.
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -19,7 +20,12 @@ namespace {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+std::atomic<int> g_weight_prefetch{1};
+
 }  // namespace
+
+void set_weight_prefetch(bool on) { g_weight_prefetch.store(on ? 1 : 0); }
+bool weight_prefetch() { return g_weight_prefetch.load() != 0; }
 
 bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, StreamPlan* plan) {
   const int pp = 32 / bits;
@@ -139,7 +145,8 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   return true;
 }
 
-cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t stream) {
+cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t stream,
+                          unsigned long long wait_ns, bool starve) {
   StreamParams p;
   p.x = a.x;
   p.qw = a.qweight;
@@ -171,6 +178,9 @@ cudaError_t launch_stream(const GemvArgs& a, const StreamPlan& pl, cudaStream_t 
   p.off_zero = pl.off_zero;
   p.C = pl.C;
   p.KC = pl.KC;
+  p.prefetch = weight_prefetch() ? 1 : 0;
+  p.starve = starve ? 1 : 0;
+  p.wait_ns = wait_ns ? wait_ns : 2000000000ull;  // 2 s: orders above any healthy wait
   const long long total = static_cast<long long>(a.N) * p.G;
   p.tail_first = total / 8 * 8;
   p.tail_n = static_cast<int>(total - p.tail_first);

@@ -10,13 +10,15 @@
 //   * warp 0 (producer) streams the CTA's rows as (16-row tile, K slab)
 //     stages into a ring of shared-memory slots: one bulk copy
 //     (cp.async.bulk, no multicast) per packed row segment, plus each tile's
-//     scales/zero-points as one contiguous span. The activations are copied
-//     first, right after the programmatic-dependent-launch wait (a copy issued
-//     behind weight copies would wait for them), then the weight ring.
-//   * warps 2.. (consumers) first rewrite the resident activations in place
-//     into the tensor-core B-fragment order and take per-step sums; then, per
-//     stage, unpack codes in registers and run mma.m16n8k16 (fp16 x fp16 ->
-//     fp32) with 16 weight rows as the M side.
+//     scales/zero-points as one contiguous span. The first ring is issued at
+//     once, before the programmatic-dependent-launch wait (weights are not
+//     written by the previous grid), so it streams while that grid drains.
+//   * warps 2.. (consumers) load the activations with plain global loads
+//     after the dependent-launch wait (off the bulk-copy queue, so they never
+//     wait behind the weight ring), store them into shared memory in the
+//     tensor-core B-fragment order and take per-step sums; then, per stage,
+//     unpack codes in registers and run mma.m16n8k16 (fp16 x fp16 -> fp32)
+//     with 16 weight rows as the M side.
 //   * warp 1 (reducer) sums the consumer warps' partials of each tile in a
 //     fixed order and writes y.
 //
@@ -155,6 +157,21 @@ __device__ __forceinline__ void lds(const uint8_t* p, uint32_t* r) {
   }
 }
 
+// NB bytes (8, 16 or 32) from global memory into registers, cached in L2 only
+// (never a stale L1 line of data the previous grid wrote).
+template <int NB>
+__device__ __forceinline__ void ldg_l2(const uint8_t* p, uint32_t* r) {
+  if constexpr (NB == 8) {
+    asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "l"(p));
+  } else {
+#pragma unroll
+    for (int i = 0; i < NB / 16; ++i)
+      asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(r[4 * i]), "=r"(r[4 * i + 1]), "=r"(r[4 * i + 2]), "=r"(r[4 * i + 3])
+                   : "l"(p + 16 * i));
+  }
+}
+
 template <int NB>
 __device__ __forceinline__ void sts(uint8_t* p, const uint32_t* r) {
   if constexpr (NB == 8) {
@@ -250,13 +267,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint64_t* meta_full = empty + kMaxStages;     // [kStreamMaxMeta]
   uint64_t* red_full = meta_full + kStreamMaxMeta;  // [kStreamNRB]
   uint64_t* red_empty = red_full + kStreamNRB;  // [kStreamNRB]
-  uint64_t* x_full = red_empty + kStreamNRB;
-  uint64_t* sx_ready = x_full + 1;              // activation sums written (reducer)
+  uint64_t* sx_ready = red_empty + kStreamNRB;  // activation sums written (reducer)
   uint64_t* xfull = sx_ready + 1;               // [kStreamNRB] peers' partials landed (rank 0)
   uint64_t* xempty = xfull + kStreamNRB;        // [kStreamNRB] rank 0 done with a slot (rank > 0)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint64_t lim = p.wait_ns;  // limit of every bounded wait
   const int S = p.stages;
   const int NMB = p.n_meta;
   // Split K: a cluster of C CTAs shares the same rows; CTA `rank` streams the
@@ -285,7 +302,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       mbar_init(&red_full[b], kStreamNCW);
       mbar_init(&red_empty[b], 1);
     }
-    mbar_init(x_full, 1);
     mbar_init(sx_ready, 1);
     for (int b = 0; b < kStreamNRB; ++b) {
       mbar_init(&xfull[b], 32 * (C - 1));
@@ -298,8 +314,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   if (C > 1) cluster_sync_all();
   if (threadIdx.x == 0) pdl_launch_dependents();
 
-  if (warp == 0) {
+  // Each role runs as a lambda: a role that gives up a bounded wait returns
+  // from its lambda and still reaches the cluster barrier below.
+  if (warp == 0) [&] {
     // ------------------------------------------------------------ producer
+    if (p.starve) return;  // diagnostic: issue nothing, every wait gives up
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
     const uint8_t* qw = reinterpret_cast<const uint8_t*>(p.qw);
@@ -358,38 +377,35 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         bulk_g2s(st + lane * p.w_pitch, qw + (r0 + lane) * row_bytes + k0 * BITS / 8, run,
                  &full[slot], pol_w);
     };
-    // Weights and metadata do not depend on the previous grid, activations
-    // may; but nothing can be computed before the activations land, and their
-    // copy would queue behind any weight copies issued ahead of it. So the
-    // activations go first, right after the wait, then the ring.
-    const int pre = 0;
-    for (int s = 0; s < pre; ++s) issue_stage(s);
-    pdl_wait_prior_grid();
-    if (lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(p.M) * kn * 2);
-    __syncwarp();
-    if (lane < p.M)
-      bulk_g2s(smem + p.off_x + lane * p.xp, p.x + static_cast<int64_t>(lane) * p.K + klo,
-               static_cast<uint32_t>(kn) * 2, x_full, pol_x);
-    int s = pre;
+    // Packed weights and metadata are inputs the previous grid does not
+    // write; the activations are loaded by the consumer warps with plain
+    // loads after their own dependent-launch wait, so nothing queues behind
+    // these copies. With p.prefetch the whole first ring is issued at once,
+    // before this grid's dependency on the previous one is resolved (the
+    // copies run while the previous grid drains); without it the producer
+    // waits for the previous grid first.
+    if (!p.prefetch) pdl_wait_prior_grid();
+    int s = 0;
+    for (; s < total && s < S && s / n_slabs < NMB; ++s) issue_stage(s);
     for (; s < total; ++s) {
       const int slot = s % S;
-      if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1)) break;
+      if (s >= S && !warp_wait(&empty[slot], ((s / S) - 1) & 1, lim)) break;
       const int i = s / n_slabs;
       if (i >= NMB && s == i * n_slabs) {
         // Metadata buffer i % NMB is free once tile i - NMB is consumed: its
         // last stage t released (implied by the wait above when t <= s - S).
         const int t = (i - NMB + 1) * n_slabs - 1;
-        if (t > s - S && !warp_wait(&empty[t % S], (t / S) & 1)) break;
+        if (t > s - S && !warp_wait(&empty[t % S], (t / S) & 1, lim)) break;
       }
       issue_stage(s);
     }
     // Drain: every copy this warp issued has landed before the CTA exits.
-    for (int t = max(0, s - S); t < s; ++t) mbar_wait(&full[t % S], (t / S) & 1);
+    for (int t = max(0, s - S); t < s; ++t) mbar_wait(&full[t % S], (t / S) & 1, lim);
     const int issued_tiles = (s + n_slabs - 1) / n_slabs;
     for (int ii = max(0, issued_tiles - NMB); ii < issued_tiles; ++ii)
-      mbar_wait(&meta_full[ii % NMB], (ii / NMB) & 1);
-    mbar_wait(x_full, 0);
-  } else if (warp == 1) {
+      mbar_wait(&meta_full[ii % NMB], (ii / NMB) & 1, lim);
+  }();
+  else if (warp == 1) [&] {
     // ------------------------------------------------------------- reducer
     const float* sxg = reinterpret_cast<const float*>(smem + p.off_sx);
     for (int i = 0; i < n_tiles; ++i) {
@@ -404,9 +420,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           zc = SYM ? kBias : __half2float(__ushort_as_half(p.zeros[r0 + lane]));
         }
       }
-      if (!warp_wait(&red_full[b], (i / kStreamNRB) & 1)) return;
+      if (!warp_wait(&red_full[b], (i / kStreamNRB) & 1, lim)) return;
       if constexpr (!GROUPED) {
-        if (!warp_wait(sx_ready, 0)) return;
+        if (!warp_wait(sx_ready, 0, lim)) return;
       }
       const float* red = reinterpret_cast<const float*>(smem + p.off_red) +
                          b * (kStreamNCW * kTile * p.M);
@@ -435,7 +451,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       if (C > 1 && rank > 0) {
         // Send the partial to rank 0's slot b (free once rank 0 released it
         // for tile i - kStreamNRB), then arrive there.
-        if (i >= kStreamNRB && !warp_wait_cluster(&xempty[b], ((i / kStreamNRB) - 1) & 1))
+        if (i >= kStreamNRB && !warp_wait_cluster(&xempty[b], ((i / kStreamNRB) - 1) & 1, lim))
           return;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -448,7 +464,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         mbar_arrive_remote(map_to_rank(&xfull[b], 0));
         continue;
       }
-      if (C > 1 && !warp_wait_cluster(&xfull[b], (i / kStreamNRB) & 1)) return;
+      if (C > 1 && !warp_wait_cluster(&xfull[b], (i / kStreamNRB) & 1, lim)) return;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int idx = q * 32 + lane;
@@ -469,9 +485,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // remote arrive can target a CTA that has exited.
     if (C > 1 && rank > 0) {
       for (int i = max(0, n_tiles - kStreamNRB); i < n_tiles; ++i)
-        if (!warp_wait_cluster(&xempty[i % kStreamNRB], (i / kStreamNRB) & 1)) return;
+        if (!warp_wait_cluster(&xempty[i % kStreamNRB], (i / kStreamNRB) & 1, lim)) return;
     }
-  } else {
+  }();
+  else [&] {
     // ----------------------------------------------------------- consumers
     using XU = XUnits<BITS, WPL>;
     const int cw = warp - 2;
@@ -483,18 +500,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const int Gs = GROUPED ? kn / p.gsize : 1;  // groups in the slice
     const int g_lo = GROUPED ? klo / p.gsize : 0;
 
-    // Prologue 1: activations, in place, into B-fragment order, with per-step
-    // sums (asymmetric formats only). Each lane takes one word per chunk of
-    // 32, four chunks per pass. Rows and steps start on multiples of SW words
-    // and chunks on multiples of 32, so a step's SW words are all in one chunk
-    // of one warp: every lane has loaded its words before any lane overwrites
-    // them. A step's sum is the sum of its quads' totals (quad_sum).
-    // The consumer warps synchronise the prologue with a named barrier (id 1):
-    // every consumer warp reaches both barriers, also when its activation
-    // wait gave up, so that none is left waiting; such a warp returns after.
+    // Prologue 1: activations from global memory into B-fragment order in
+    // shared memory, with per-step sums (asymmetric formats only). The loads
+    // come after this thread's dependent-launch wait (the previous grid may
+    // have written x) and use the load/store path, not the bulk-copy queue
+    // that carries the weight ring. The words of all M rows form one flat
+    // index space; each lane loads kU words (128 bytes) per pass. Rows and
+    // steps start on multiples of SW words and each pass's words are
+    // contiguous in groups of 32 lanes, so a step's SW words lie in one
+    // aligned group of SW lanes; a step's sum is the sum of its quads'
+    // totals (quad_sum).
     for (int i = tid; i < STEP_XB / 16; i += kCT)
       reinterpret_cast<uint4*>(smem + p.off_zero)[i] = make_uint4(0u, 0u, 0u, 0u);
-    const bool x_ok_wait = warp_wait(x_full, 0);
+    pdl_wait_prior_grid();
     // Word wi of an activation row, permuted in registers and stored at its
     // place in the row's B-fragment order.
     auto put = [&](const uint32_t (&w)[NPAIR], uint8_t* row, int wi) {
@@ -517,59 +535,37 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         sts<PB>(sbase + (lb / XU::U) * 4 * XU::U + (lb % XU::U), o + pc * (PB / 4));
       }
     };
-    constexpr int kU = 4;
+    constexpr int kU = 128 / WB;
     const int wpr = kn / PP;  // words per activation row
-    if (!x_ok_wait) {
-    } else if constexpr (SYM) {
-      // No sums: row by row (measured faster than the flat order below for
-      // the symmetric formats).
-      for (int m = 0; m < p.M; ++m) {
-        uint8_t* row = smem + p.off_x + m * p.xp;
-        for (int w0 = cw * 32; w0 < wpr; w0 += kU * kCT) {
-          uint32_t v[kU][NPAIR];
+    const int wtot = p.M * wpr;
+    const uint8_t* xg = reinterpret_cast<const uint8_t*>(p.x + klo);
+    const int64_t xrow_bytes = static_cast<int64_t>(p.K) * 2;
+    // ceil(2^32 / wpr): umulhi(f, wmagic) == f / wpr for every f < 2^32 / wpr.
+    const uint32_t wmagic = 0xFFFFFFFFu / static_cast<uint32_t>(wpr) + 1u;
+    for (int w0 = cw * 32; w0 < wtot; w0 += kU * kCT) {
+      uint32_t v[kU][NPAIR];
+      int mrow[kU], wcol[kU];
 #pragma unroll
-          for (int uu = 0; uu < kU; ++uu) {
-            const int wi = w0 + uu * kCT + lane;
-            if (wi < wpr) lds<WB>(row + wi * WB, v[uu]);
-          }
-          __syncwarp();
+      for (int uu = 0; uu < kU; ++uu) {
+        const int wf = w0 + uu * kCT + lane;
+        const int m = static_cast<int>(__umulhi(static_cast<uint32_t>(wf), wmagic));
+        mrow[uu] = m;
+        wcol[uu] = wf - m * wpr;
+        if (wf < wtot) {
+          ldg_l2<WB>(xg + m * xrow_bytes + wcol[uu] * WB, v[uu]);
+        } else {
 #pragma unroll
-          for (int uu = 0; uu < kU; ++uu) {
-            const int wi = w0 + uu * kCT + lane;
-            if (wi < wpr) put(v[uu], row, wi);
-          }
+          for (int r = 0; r < NPAIR; ++r) v[uu][r] = 0u;
         }
       }
-    } else {
-      // The words of all M rows as one flat index space (fewer, fuller passes
-      // when a row has fewer than 4 x 256 words).
-      const int wtot = p.M * wpr;
-      // ceil(2^32 / wpr): umulhi(f, wmagic) == f / wpr for every f < 2^32 / wpr.
-      const uint32_t wmagic = 0xFFFFFFFFu / static_cast<uint32_t>(wpr) + 1u;
-      for (int w0 = cw * 32; w0 < wtot; w0 += kU * kCT) {
-        uint32_t v[kU][NPAIR];
-        int mrow[kU], wcol[kU];
 #pragma unroll
-        for (int uu = 0; uu < kU; ++uu) {
-          const int wf = w0 + uu * kCT + lane;
-          const int m = static_cast<int>(__umulhi(static_cast<uint32_t>(wf), wmagic));
-          mrow[uu] = m;
-          wcol[uu] = wf - m * wpr;
-          if (wf < wtot) {
-            lds<WB>(smem + p.off_x + m * p.xp + wcol[uu] * WB, v[uu]);
-          } else {
-#pragma unroll
-            for (int r = 0; r < NPAIR; ++r) v[uu][r] = 0u;
-          }
-        }
+      for (int uu = 0; uu < kU; ++uu) {
+        if (w0 + uu * kCT + lane < wtot) put(v[uu], smem + p.off_x + mrow[uu] * p.xp, wcol[uu]);
+      }
+      if constexpr (!SYM) {
         float sum[kU];
 #pragma unroll
         for (int uu = 0; uu < kU; ++uu) sum[uu] = quad_sum<NPAIR>(v[uu]);
-        __syncwarp();
-#pragma unroll
-        for (int uu = 0; uu < kU; ++uu) {
-          if (w0 + uu * kCT + lane < wtot) put(v[uu], smem + p.off_x + mrow[uu] * p.xp, wcol[uu]);
-        }
 #pragma unroll
         for (int off = SW / 2; off >= 4; off >>= 1)
 #pragma unroll
@@ -585,7 +581,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // Prologue 2: the activation sum of every group (per-channel: of the
     // whole row); symmetric formats need none.
     if constexpr (SYM) {
-    } else if (!x_ok_wait) {
     } else if constexpr (GROUPED) {
       const int spg = p.gsize / SC;
       for (int e = tid; e < p.M * Gs; e += kCT) {
@@ -607,7 +602,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     named_sync(1, kStreamNCW * 32);
     if (tid == 0) mbar_arrive(sx_ready);
-    if (!x_ok_wait) return;
 
     // Main loop. Work units (grouped: gslots consecutive groups; per-channel:
     // one step) go to warps round-robin by their index over the whole CTA.
@@ -637,7 +631,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const int r0 = row_begin + i * kTile;
       // (Waited for in every mode: the producer reuses a metadata buffer
       // only after its previous copy has been seen complete here.)
-      if (!warp_wait(&meta_full[i % NMB], (i / NMB) & 1)) return;
+      if (!warp_wait(&meta_full[i % NMB], (i / NMB) & 1, lim)) return;
       const uint8_t* meta = smem + p.off_meta + (i % NMB) * p.meta_stride;
       const int64_t a0 = (static_cast<int64_t>(r0) * p.G * 2) & ~15ll;
       // Byte offsets of (row gid, group 0) and (row gid + 8, group 0).
@@ -645,7 +639,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       const int mo_b = mo_a + 8 * p.G * 2;
       for (int j = 0; j < n_slabs; ++j, ++s) {
         const int slot = s % S;
-        if (!warp_wait(&full[slot], (s / S) & 1)) return;
+        if (!warp_wait(&full[slot], (s / S) & 1, lim)) return;
         const int k0 = klo + j * p.KS;          // absolute K of the slab
         const int L = min(p.KS, klo + kn - k0);
         const int kx0 = k0 - klo;               // its offset in the resident slice
@@ -800,7 +794,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         for (int e = 0; e < 4; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 2);
       }
       const int b = i % kStreamNRB;
-      if (i >= kStreamNRB && !warp_wait(&red_empty[b], ((i / kStreamNRB) - 1) & 1)) return;
+      if (i >= kStreamNRB && !warp_wait(&red_empty[b], ((i / kStreamNRB) - 1) & 1, lim)) return;
       float* red = reinterpret_cast<float*>(smem + p.off_red) + b * (kStreamNCW * kTile * p.M) +
                    cw * kTile * p.M;
       const int cmask = mp <= 2 ? 3 : (mp == 4 ? 2 : 0);
@@ -817,7 +811,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[b]);
     }
-  }
+  }();
+  // No CTA of a cluster exits while a peer may still store into its shared
+  // memory or arrive on its barriers: all threads of all CTAs meet here, also
+  // after a wait gave up (every wait before this point is bounded).
+  if (C > 1) cluster_sync_all_unaligned();
 }
 
 

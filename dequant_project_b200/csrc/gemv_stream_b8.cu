@@ -9,3 +9,5 @@ cudaError_t launch_stream_b8(int wpl, int gs, bool sym, bool inter, const Stream
 }
 
 }  // namespace dqg
+
+DQG_STATUS_READER(read_status_stream_b8)

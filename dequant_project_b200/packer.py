@@ -52,17 +52,17 @@ class QuantConfig:
 
     @property
     def per_pack(self):
-        """Codes packed into one 32-bit word."""
+        """32 / bits: how many codes one int32 word carries."""
         return 32 // self.bits
 
     @property
     def qmax(self):
-        """Largest storable unsigned code."""
+        """2^bits - 1, the top of the code range."""
         return (1 << self.bits) - 1
 
     @property
     def bias(self):
-        """Offset added to symmetric codes so that they store unsigned."""
+        """2^(bits-1): symmetric codes are stored as q + this, so they fit unsigned."""
         return 1 << (self.bits - 1)
 
     def groups_for(self, k):
@@ -74,7 +74,8 @@ class QuantConfig:
 
 @dataclass
 class PackedWeight:
-    """A quantized weight plus what is needed to reconstruct it (packer.py:81-96)."""
+    """Packed codes, per-group scales and (asymmetric) zero-points of one
+    [N, K] weight, with its format and shape (packer.py:81-96)."""
 
     qweight: torch.Tensor          # int32 [N, K // per_pack] (uint32 bit patterns)
     scales: torch.Tensor           # fp16  [N, n_groups]

@@ -1,18 +1,21 @@
-"""The packed weight as a drop-in ``nn.Linear`` replacement.
+"""Packed weights behind an ``nn.Linear``-shaped module.
 
-Mirrors KrishnaI2424/Dequant_Project ``dequant/quant_linear.py`` (public names
-``MAX_M``, ``PROJ``, ``gemv``, ``dequantize_cuda``, ``QuantLinear``,
-``quantize_model``; same semantics), backed by the B200 kernels of this
-package instead of the reference's extension:
+Public surface of KrishnaI2424/Dequant_Project ``dequant/quant_linear.py``
+(``MAX_M``, ``PROJ``, ``gemv``, ``dequantize_cuda``, ``QuantLinear`` with
+buffers ``qweight/scales/zeros/bias`` and ``from_linear``, ``quantize_model``
+returning ``{"replaced", "packed_bytes", "fp16_bytes"}``), served by the B200
+kernels of this package. Which kernel runs depends on the number of activation
+rows ``M`` (all leading dimensions of ``x`` flattened):
 
-    M <= MAX_M   fused dequant + GEMV (tensor-core MMA over in-register
-                 unpacked codes); weights cross HBM packed.
-    M >  MAX_M   materialise the fp16 weight with the bit-exact dequantize
-                 kernel and call F.linear (cuBLAS), as the reference does
-                 (quant_linear.py:126-135).
+* ``M <= MAX_M``: the fused dequant + GEMV; the weight crosses HBM packed.
+* ``M >  MAX_M``: the bit-exact dequantize kernel materialises the fp16 weight
+  and ``F.linear`` multiplies (prefill is compute-bound; the reference takes
+  the same route, ``quant_linear.py:126-135``).
 
-``forward`` never touches the CPU and never synchronises, so decode steps built
-from these modules are CUDA-graph capturable.
+Nothing here synchronises or reads device data on the host, so modules built
+from it can be captured in CUDA graphs. A module keeps the kernel arguments of
+its format (bits, group size, symmetry, slot order) from construction on, so a
+call costs one binding call and no per-call object construction.
 """
 
 from __future__ import annotations
@@ -24,90 +27,114 @@ from torch import nn
 from dequant_project_b200 import dequant_cuda as _ext
 from dequant_project_b200.packer import PackedWeight, QuantConfig, quantize_tensor
 
-# Largest activation row count the fused GEMV handles (quant_linear.py:38-39).
+#: Most activation rows the fused GEMV takes in one call.
 MAX_M = _ext.MAX_M
 
-# The seven projections per decoder layer that are quantized; norms, embeddings
-# and the LM head stay fp16 (quant_linear.py:41-44).
+#: Leaf names of the linear layers ``quantize_model`` packs by default: the
+#: attention and MLP projections of a Llama-style layer. Embeddings, norms and
+#: the LM head are left alone.
 PROJ = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
 
 
-def gemv(x, pw: PackedWeight):
-    """y = x @ W^T with W held packed. x is [..., K] fp16, y is [..., N] fp16."""
+def _format_args(cfg: QuantConfig, in_features: int) -> tuple:
+    """(bits, group_size, symmetric, interleaved) as the kernels take them;
+    per-channel formats pass the whole row as one group."""
+    return (cfg.bits, cfg.effective_group_size(in_features), bool(cfg.symmetric),
+            cfg.layout == "interleaved")
+
+
+def _rows(x: torch.Tensor, k: int) -> torch.Tensor:
+    """``x`` as a contiguous [M, K] matrix."""
+    return x.reshape(-1, k).contiguous()
+
+
+def gemv(x: torch.Tensor, pw: PackedWeight) -> torch.Tensor:
+    """``x @ W^T`` for a packed ``W`` [N, K]: ``x`` fp16 [..., K] with at most
+    ``MAX_M`` rows in total, result fp16 [..., N]."""
     n, k = pw.shape
-    cfg = pw.config
-    x2 = x.reshape(-1, k).contiguous()
-    y = _ext.gemv(x2, pw.qweight, pw.scales, pw.zeros, cfg.bits, cfg.effective_group_size(k),
-                  cfg.symmetric, cfg.layout == "interleaved")
+    y = _ext.gemv(_rows(x, k), pw.qweight, pw.scales, pw.zeros, *_format_args(pw.config, k))
     return y.view(*x.shape[:-1], n)
 
 
-def dequantize_cuda(pw: PackedWeight):
-    """Reconstruct the fp16 [N, K] weight on the GPU, bit-exact with the packer."""
+def dequantize_cuda(pw: PackedWeight) -> torch.Tensor:
+    """The fp16 [N, K] weight rebuilt on the GPU, bit for bit what the packer's
+    ``dequantize`` gives."""
     n, k = pw.shape
-    cfg = pw.config
-    return _ext.dequantize(pw.qweight, pw.scales, pw.zeros, cfg.bits,
-                           cfg.effective_group_size(k), cfg.symmetric,
-                           cfg.layout == "interleaved", k)
+    return _ext.dequantize(pw.qweight, pw.scales, pw.zeros, *_format_args(pw.config, k), k)
 
 
 class QuantLinear(nn.Module):
-    """nn.Linear whose weight lives only in packed form (quant_linear.py:96-140)."""
+    """A linear layer that holds its weight only as packed codes, fp16 scales
+    and (asymmetric formats) fp16 zero-points; ``bias`` is optional fp16."""
 
-    def __init__(self, pw: PackedWeight, bias=None):
+    def __init__(self, pw: PackedWeight, bias: torch.Tensor | None = None):
         super().__init__()
         self.out_features, self.in_features = pw.shape
         self.config = pw.config
-        self.register_buffer("qweight", pw.qweight)
-        self.register_buffer("scales", pw.scales)
-        self.register_buffer("zeros", pw.zeros)
-        self.register_buffer("bias", bias)
+        self._kargs = _format_args(pw.config, self.in_features)
+        # Buffers, so that .to() / .cuda() / state_dict carry them.
+        for name, t in (("qweight", pw.qweight), ("scales", pw.scales), ("zeros", pw.zeros),
+                        ("bias", bias)):
+            self.register_buffer(name, t)
 
     @classmethod
-    def from_linear(cls, linear: nn.Linear, cfg: QuantConfig):
-        pw = quantize_tensor(linear.weight.data, cfg)
-        bias = None if linear.bias is None else linear.bias.data.to(torch.float16)
-        return cls(pw, bias)
+    def from_linear(cls, linear: nn.Linear, cfg: QuantConfig) -> "QuantLinear":
+        """Quantize and pack ``linear``'s weight (on its device) with ``cfg``."""
+        bias = linear.bias
+        return cls(quantize_tensor(linear.weight.detach(), cfg),
+                   None if bias is None else bias.detach().to(torch.float16))
 
-    def _packed(self):
-        # Rebuilt per call so that .to()/.cuda() buffer moves stay correct.
+    def _packed(self) -> PackedWeight:
+        """The buffers as a ``PackedWeight`` (views, no copies)."""
         return PackedWeight(qweight=self.qweight, scales=self.scales, zeros=self.zeros,
                             config=self.config, shape=(self.out_features, self.in_features))
 
-    def forward(self, x):
-        pw = self._packed()
-        m = x.numel() // self.in_features
-        if m <= MAX_M:
-            y = gemv(x, pw)
-        else:
-            y = F.linear(x, dequantize_cuda(pw))
-        if self.bias is not None:
-            y = y + self.bias
-        return y
+    def packed_nbytes(self) -> int:
+        """Bytes of the packed weight: codes, scales and zero-points."""
+        return sum(t.numel() * t.element_size()
+                   for t in (self.qweight, self.scales, self.zeros) if t is not None)
 
-    def extra_repr(self):
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        k = self.in_features
+        x2 = _rows(x, k)
+        if x2.shape[0] <= MAX_M:
+            y2 = _ext.gemv(x2, self.qweight, self.scales, self.zeros, *self._kargs)
+        else:
+            w = _ext.dequantize(self.qweight, self.scales, self.zeros, *self._kargs, k)
+            y2 = F.linear(x2, w)
+        y = y2.view(*x.shape[:-1], self.out_features)
+        return y if self.bias is None else y + self.bias
+
+    def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bias={self.bias is not None}, config={self.config}")
 
 
-def quantize_model(model, cfg: QuantConfig, names=PROJ):
-    """Replace every nn.Linear named in `names` with a QuantLinear, in place.
+def quantize_model(model: nn.Module, cfg: QuantConfig, names=PROJ) -> dict:
+    """Swap, in place, every ``nn.Linear`` whose attribute name is in ``names``
+    for a ``QuantLinear`` packed with ``cfg``; every other module is left as it
+    is. Returns how many were swapped and the bytes of their packed and fp16
+    weights."""
+    wanted = frozenset(names)
+    stats = {"replaced": 0, "packed_bytes": 0, "fp16_bytes": 0}
+    visited: set[int] = set()
 
-    Returns {"replaced", "packed_bytes", "fp16_bytes"} (quant_linear.py:143-162).
-    """
-    replaced = 0
-    packed_bytes = 0
-    fp16_bytes = 0
-    for path, mod in list(model.named_modules()):
-        leaf = path.rsplit(".", 1)[-1]
-        if leaf not in names or not isinstance(mod, nn.Linear):
-            continue
-        parent = model.get_submodule(path.rsplit(".", 1)[0] if "." in path else "")
-        ql = QuantLinear.from_linear(mod, cfg)
-        setattr(parent, leaf, ql)
-        replaced += 1
-        packed_bytes += ql._packed().nbytes
-        fp16_bytes += mod.weight.numel() * 2
+    def visit(parent: nn.Module) -> None:
+        if id(parent) in visited:
+            return
+        visited.add(id(parent))
+        for attr, child in list(parent.named_children()):
+            if attr in wanted and isinstance(child, nn.Linear):
+                q = QuantLinear.from_linear(child, cfg)
+                setattr(parent, attr, q)
+                stats["replaced"] += 1
+                stats["packed_bytes"] += q.packed_nbytes()
+                stats["fp16_bytes"] += 2 * child.weight.numel()
+            else:
+                visit(child)
+
+    visit(model)
+    # The replaced fp16 weights are garbage now; hand their blocks back.
     if torch.cuda.is_available():
         torch.cuda.empty_cache()
-    return {"replaced": replaced, "packed_bytes": packed_bytes, "fp16_bytes": fp16_bytes}
+    return stats

@@ -63,7 +63,10 @@ int dqg_add_one(const float *x, float *out, int64_t n, void *stream);
  *   group_size % (128 / bits) == 0 (so INT2 with group 32 is rejected);
  *   zeros != NULL exactly when symmetric == 0; x 16-byte aligned.
  * Additionally qweight must be 16-byte aligned (it is streamed with bulk
- * copies). group_size == K is per-channel quantisation.
+ * copies). group_size == K is per-channel quantisation. Whether each pointer
+ * is device memory of the current device is checked only when the
+ * environment variable DQG_CHECK_POINTERS is set (those queries cost about as
+ * much as a small GEMV); see also dqg_set_weight_prefetch.
  */
 int dqg_gemv(const void *x, const int32_t *qweight, const void *scales, const void *zeros,
              void *y, int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
@@ -81,12 +84,40 @@ int dqg_dequantize(const int32_t *qweight, const void *scales, const void *zeros
                    int interleaved, void *stream);
 
 /*
- * Device-side status word of `device` (bit 0: a kernel gave up a bounded
- * wait). Synchronous; for tests and diagnostics, not for the hot path.
+ * Device-side status of `device` (bit 0: a kernel of this library gave up a
+ * bounded wait), the OR of the status words of all its kernels. Synchronous;
+ * for tests and diagnostics, not for the hot path.
  * If reset != 0 the word is cleared after reading. No reference counterpart:
  * the reference kernels have no waits.
  */
 int dqg_device_status(int device, uint32_t *status, int reset);
+
+/*
+ * Process-wide switch, default on; returns the previous setting. When on,
+ * dqg_gemv's streaming kernel issues its first ring of packed-weight copies
+ * (qweight, scales, zeros) before it waits for the kernel that precedes it on
+ * the stream, so those copies overlap that kernel's tail (programmatic
+ * dependent launch; the activations are always read after the wait). The
+ * packed weight must then not be written by the immediately preceding kernel
+ * if that kernel lets dependent launches start early (griddepcontrol
+ * launch_dependents); kernels that do not (every torch kernel) complete
+ * before the GEMV starts. Turn it off for weights produced that way. No
+ * reference counterpart: the reference kernel has no dependent launch.
+ */
+int dqg_set_weight_prefetch(int enable);
+
+/*
+ * Diagnostic for the bounded-wait path: launches the streaming GEMV kernel for
+ * this shape with its copy-issuing warp doing nothing, so that every wait in
+ * the kernel gives up after wait_ns (1 ms to 1 s) and the kernel returns with
+ * bit 0 set in the device status word (dqg_device_status); y is left
+ * unwritten. Only shapes whose plan is a single CTA per row block (no split-K
+ * cluster) are accepted. For tests; no reference counterpart.
+ */
+int dqg_debug_gemv_starved(const int32_t *qweight, const void *scales, const void *zeros,
+                           void *y, const void *x, int64_t M, int64_t N, int64_t K,
+                           int64_t bits, int64_t group_size, int symmetric, int interleaved,
+                           uint64_t wait_ns, void *stream);
 
 /*
  * The streaming GEMV kernel's launch plan for a shape (host arithmetic only,

@@ -1,7 +1,7 @@
 """One GEMV case as a profiling workload (for ncu and similar tools).
 
-    python -m dequant_project_b200.profile_case --n 4096 --k 11008 --bits 4 \
-        --group-size 128 --m 1 [--asym] [--copies 8] [--launches 4]
+    python tests/profile_case.py --n 4096 --k 11008 --bits 4 \
+        --group-size 128 --m 1 [--sym] [--copies 8] [--launches 6]
 
 Quantizes `copies` distinct random weights ~N(0, 0.02) of shape [n, k] with
 the packer, then launches `launches` GEMVs through the public
@@ -14,6 +14,10 @@ L2). The first `--warm` launches are warm-up; profile the ones after them with
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 
 def main() -> None:

@@ -76,3 +76,21 @@ def test_binding_validates_like_the_reference():
         dequant_cuda.add_one(torch.ones(4))
     with pytest.raises(RuntimeError, match="bits must be 2, 4 or 8"):
         dequant_cuda.dequantize(qw, s, None, 3, 128, True, False, 512)
+
+
+def test_starved_diagnostic_rejects_bad_limits_without_a_gpu():
+    lib = _native.lib()
+    for wait_ns in (0, 10, 2_000_000_000):
+        rc = lib.dqg_debug_gemv_starved(16, 16, 16, 16, 16, 1, 64, 512, 4, 128, 0, 0, wait_ns,
+                                        None)
+        assert rc == 1 and b"wait_ns must be in" in lib.dqg_last_error()
+
+
+def test_weight_prefetch_switch_round_trips():
+    lib = _native.lib()
+    prev = lib.dqg_set_weight_prefetch(0)
+    try:
+        assert lib.dqg_set_weight_prefetch(1) == 0
+        assert lib.dqg_set_weight_prefetch(1) == 1
+    finally:
+        lib.dqg_set_weight_prefetch(prev)
