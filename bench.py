@@ -1,35 +1,35 @@
 #!/usr/bin/env python
-"""Benchmark of the fused low-bit dequant + GEMV path on B200.
+"""Benchmark of the fused low-bit dequant + GEMV decode path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU)
 
-Workload (the bit-width sweep): GEMV with W 4096x11008 and
-11008x4096, quantized INT8 per-channel symmetric, INT4 group-128 asymmetric
-and INT2 group-64 asymmetric, activations x fp16 [M, K] for M = 1, 4, 8 -- 18
-cases. Weights are random-init ~N(0, 0.02) quantized by the product packer,
-activations ~N(0, 1) (synthetic; the reference has no dataset). Every case has
-its own packed tensors, so one step touches ~480 MB of distinct weights, far
-more than the 126 MB L2: no case is served from L2.
+Headline (every N): decode tokens/s of a Llama-2-7B
+architecture decoder whose every linear layer and the LM head are INT4 g128
+packed, batch 1, 2048-token fp16 KV cache, tensor-parallel over the N ranks
+(column-parallel QKV and gate/up, row-parallel O and down with an all-reduce
+over peer memory, vocabulary-parallel LM head). One step = one token; the
+same model and token at every N, so ``scaling`` is "strong" and the driver's
+efficiency is the decode step's. Weights are random-init ~N(0, 0.02) (no
+checkpoints offline), 3.5 GB packed: far larger than the 126 MB L2. The step
+is replayed from a CUDA graph, timed with CUDA events, max over ranks.
 
-One step = the 18 GEMVs once, replayed from one CUDA graph. ``value`` is the
-whole-job achieved HBM bandwidth, algorithmic bytes (byte_model.gemv_bytes)
-over device time, summed over ranks (each rank runs its own sweep: weak
-scaling, no collective on the data path). ``e2e`` is the same metric through
-the public ``dequant_cuda.gemv`` call with the activations copied from pinned
-host memory and the outputs copied back inside the timed region.
+``roofline`` is the dominant kernel of that step, the fused dequant + GEMV:
+the step's GEMVs alone (same shapes, weights and order, their own graph),
+algorithmic bytes over device time against the measured HBM copy bandwidth.
+``e2e`` is the same step as a caller runs it: token ids copied in from pinned
+host memory, the graph replayed, the logits copied back to pinned host memory.
 
-``shape_sweep`` (one GPU) is BASELINE config 3: INT4 g128 at batch 1 over
-(4096,4096), (12288,4096), (4096,14336), (28672,8192), (8192,28672) and
-(128256,4096), per case µs and GB/s.
+Sub-keys: ``decode_batch8`` (same model, batch 8); ``decode_70b`` (N >= 2,
+Llama-3-70B architecture, INT4 g128 and INT2 g64, batch 1
+and 8, 4096-token cache); ``gemv_sweep`` (N = 1: the 18
+bit-width sweep GEMVs as one graph, with per-case µs, and ``shape_sweep``,
+BASELINE config 3).
 
-``decode`` adds decode ms/token of the tensor-parallel decoder at TP = N
-(Llama-2-7B architecture, every linear and the LM head INT4
-g128 packed, batch 1, 2048-token fp16 KV cache), from a CUDA graph of one step,
-max over ranks (dequant_project_b200/decode_bench.py).
-
-``--impl reference`` times the reference's CPU path (the C restatement of
-``F.linear(x, packer.dequantize(pw))`` in oracle/, all host threads) on a
-bounded row sample of the same 18 cases, on rank 0 only.
+``--impl reference`` times the reference's CPU path for the same token (its
+GEMVs ``F.linear(x, packer.dequantize(W))`` as the C restatement in oracle/,
+all host threads) on a bounded row sample of every matrix of one layer and the
+LM head, scaled to the whole step; rank 0 only.
 """
 
 from __future__ import annotations
@@ -47,9 +47,11 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = ("GEMV achieved HBM GB/s over the bit-width sweep "
-          "(INT8 per-ch / INT4 g128 / INT2 g64; 4096x11008 & 11008x4096; M=1,4,8)")
-UNIT = "GB/s"
+METRIC = ("decode tokens/s, Llama-2-7B architecture, all linears and LM head INT4 g128 "
+          "packed, batch 1, 2048-token KV cache, tensor-parallel over n_gpus")
+UNIT = "tokens/s"
+SWEEP_METRIC = ("GEMV achieved HBM GB/s over the bit-width sweep "
+                "(INT8 per-ch / INT4 g128 / INT2 g64; 4096x11008 & 11008x4096; M=1,4,8)")
 SHAPES = [(4096, 11008), (11008, 4096)]
 FORMATS = [(8, None, True, "int8-perch-sym"), (4, 128, False, "int4-g128-asym"),
            (2, 64, False, "int2-g64-asym")]
@@ -67,11 +69,18 @@ def case_bytes(n, k, bits, gs, sym, m):
 
 
 def workload_config(world):
+    return {"workload": "decode step (BASELINE config 4): Llama-2-7B architecture, INT4 g128 "
+                        "(asymmetric) linears and LM head, batch 1, 2048-token fp16 KV cache",
+            "tokens_per_step": 1,
+            "l2": "inputs > L2 (3.5 GB of packed weights and 1.07 GB of KV cache per step)",
+            "parallelism": f"tp{world}" if world > 1 else "tp1"}
+
+
+def sweep_config():
     return {"workload": "bit-width sweep (BASELINE config 2): 18 GEMVs/step",
             "shapes": ["4096x11008", "11008x4096"],
             "formats": [f[3] for f in FORMATS], "batches": list(BATCHES),
-            "l2": "inputs > L2 (18 distinct packed matrices, ~480 MB per step)",
-            "parallelism": f"replicas x{world} (weak)"}
+            "l2": "inputs > L2 (18 distinct packed matrices, ~480 MB per step)"}
 
 
 # --------------------------------------------------------------------- clocks
@@ -138,12 +147,88 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ our arm
 
-def run_ours(args, rank, world, local_rank):
+def gemv_sweep(args, dev, peaks):
+    """BASELINE config 2 on this GPU: the 18 sweep GEMVs, each on its own
+    packed tensors, replayed from one graph; GB/s over device time, per-case
+    µs, the shape sweep, and the same through the public call with host
+    buffers."""
     import torch
 
     from dequant_project_b200 import dequant_cuda
-    from dequant_project_b200.byte_model import measured_peaks
     from dequant_project_b200.packer import QuantConfig, quantize_tensor
+
+    cs = cases()
+    data = []
+    for i, (n, k, bits, gs, sym, m, _) in enumerate(cs):
+        g = torch.Generator(device=dev).manual_seed(1000 + i)
+        w = torch.randn(n, k, dtype=torch.float16, device=dev, generator=g) * 0.02
+        pw = quantize_tensor(w, QuantConfig(bits, gs, sym))
+        del w
+        x = torch.randn(m, k, dtype=torch.float16, device=dev, generator=g)
+        data.append((pw, x))
+    torch.cuda.synchronize()
+    step_bytes = sum(case_bytes(n, k, bits, gs, sym, m) for (n, k, bits, gs, sym, m, _) in cs)
+
+    def step():
+        for (n, k, bits, gs, sym, m, _), (pw, x) in zip(cs, data):
+            dequant_cuda.gemv(x, pw.qweight, pw.scales, pw.zeros, bits, gs or k, sym, False)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    del graph
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    out = {"metric": SWEEP_METRIC, "value": round(gbs, 2), "unit": "GB/s",
+           "ms_per_step": round(ms, 5), "config": sweep_config(),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                        "bytes_per_launch_avg": step_bytes // len(cs)}}
+    e2e = run_e2e(dev, cs, data, args, None, dev.index)
+    out["e2e"] = {"value": round(step_bytes / (e2e["ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+                  "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                  "path": "dequant_cuda.gemv (eager, pinned host x -> device -> pinned host y)"}
+    if not args.no_detail:
+        out["detail"] = per_case_detail(dev, cs, data, peaks)
+        try:
+            out["shape_sweep"] = shape_sweep(dev, peaks)
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
+            out["shape_sweep"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    if not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(cs, data, budget_s=args.cpu_seconds / 2)
+    del data
+    torch.cuda.empty_cache()
+    return out
+
+
+def decode_launches(cfg, world: int) -> int:
+    """Launches of this library's kernels in one decode step: per layer two
+    norms, four GEMVs, RoPE + KV append, attention, SwiGLU (and two peer
+    all-reduces at world > 1); then the final norm and the LM head GEMV."""
+    return cfg.n_layers * (9 + (2 if world > 1 else 0)) + 2
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    from dequant_project_b200 import decode_bench
+    from dequant_project_b200 import decoder as D
+    from dequant_project_b200.byte_model import measured_peaks
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -154,141 +239,100 @@ def run_ours(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-
-    cs = cases()
-    # Weights: one distinct packed matrix per case (so M=1/4/8 do not share L2).
-    data = []
-    for i, (n, k, bits, gs, sym, m, _) in enumerate(cs):
-        g = torch.Generator(device=dev).manual_seed(1000 * rank + i)
-        w = torch.randn(n, k, dtype=torch.float16, device=dev, generator=g) * 0.02
-        pw = quantize_tensor(w, QuantConfig(bits, gs, sym))
-        del w
-        x = torch.randn(m, k, dtype=torch.float16, device=dev, generator=g)
-        data.append((pw, x))
-    torch.cuda.synchronize()
-    step_bytes = sum(case_bytes(n, k, bits, gs, sym, m) for (n, k, bits, gs, sym, m, _) in cs)
-
-    def step():
-        ys = []
-        for (n, k, bits, gs, sym, m, _), (pw, x) in zip(cs, data):
-            ys.append(dequant_cuda.gemv(x, pw.qweight, pw.scales, pw.zeros, bits, gs or k, sym,
-                                        False))
-        return ys
-
-    # Capture one step in a CUDA graph (side-stream warm-up first).
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for _ in range(2):
-            step()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        static_ys = step()
-    del static_ys
-
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-
-    # Warm-up, including ~1 s of replays so that clocks are settled when the
-    # timed region starts; clocks are sampled throughout.
-    with ClockSampler(local_rank) as clk:
-        for _ in range(max(3, args.warmup)):
-            graph.replay()
-        torch.cuda.synchronize()
-        t_soak = time.perf_counter()
-        while time.perf_counter() - t_soak < 1.0:
-            for _ in range(50):
-                graph.replay()
-            torch.cuda.synchronize()
-        stream = torch.cuda.current_stream(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        e0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t1 = time.perf_counter()
-        barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    if dist is not None:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    clocks = clk.summary(t0 - 1.2, t1)
-
-    value = step_bytes * world / (ms * 1e-3) / 1e9
     peaks = measured_peaks()
-    per_gpu = step_bytes / (ms * 1e-3) / 1e9
 
-    # Per-case µs (the reference's method: n_copies distinct weights replayed
-    # in one graph, scripts/bench_dequant_kernel.py:119-168), rank 0, 1 GPU.
-    detail = None
-    if rank == 0 and world == 1 and not args.no_detail:
-        detail = per_case_detail(dev, cs, data, peaks)
-    shapes = None
-    if rank == 0 and world == 1 and not args.no_detail:
-        try:
-            shapes = shape_sweep(dev, peaks)
-        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
-            shapes = {"error": f"{type(exc).__name__}: {exc}"[:300]}
-
-    # End to end through the public API with host buffers.
-    e2e = run_e2e(dev, cs, data, args, dist, local_rank)
-    e2e_value = step_bytes * world / (e2e["ms"] * 1e-3) / 1e9
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cs, data, budget_s=args.cpu_seconds)
-
-    # Decode ms/token of the tensor-parallel decoder at TP = world (BASELINE
-    # config 4: Llama-2-7B architecture, INT4 g128, batch 1, 2048-token KV
-    # cache), timed the same way (CUDA events, max over ranks). A failure here
-    # is reported in the line and never voids the GEMV result.
-    decode = None
+    # Headline: BASELINE config 4 at TP = world, clocks sampled throughout.
+    dargs = decode_bench.default_args(steps=args.steps, warmup=args.warmup)
+    with ClockSampler(local_rank) as clk:
+        t0 = time.perf_counter()
+        line = decode_bench.measure(dargs, dist, rank, world, dev, parts=True, e2e=True,
+                                    check_tp1=world > 1)
+        t1 = time.perf_counter()
+    extra = {}
     if not args.no_decode:
         try:
-            from dequant_project_b200 import decode_bench
-            decode = decode_bench.measure(decode_bench.default_args(), dist, rank, world, dev)
-        except Exception as exc:  # noqa: BLE001
-            decode = {"error": f"{type(exc).__name__}: {exc}"[:300]}
-
-    traffic = load_traffic()
+            extra["decode_batch8"] = decode_bench.measure(
+                decode_bench.default_args(steps=max(20, args.steps // 4), warmup=args.warmup,
+                                          batch=8), dist, rank, world, dev, parts=False,
+                e2e=False)
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
+            extra["decode_batch8"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        if world > 1 or args.with_70b:
+            extra["decode_70b"] = decode_70b(args, dist, rank, world, dev)
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = gemv_sweep(args, dev, peaks)
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        ms = line["value"]
+        tps = 1.0 / (ms * 1e-3)
+        gemv = line.get("gemv", {})
+        out = {
+            "metric": METRIC, "value": round(tps, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp16 activations x int2/4/8 codes, fp32 accumulate",
-            "data": "synthetic (random-init N(0,0.02) weights, N(0,1) activations)",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16 activations x int4 codes, fp32 accumulate",
+            "data": "synthetic (random-init N(0,0.02) weights, N(0,1) fp16 KV cache)",
             "config": workload_config(world),
-            "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2),
-                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(per_gpu / peaks["hbm_gbs"], 4),
+            "roofline": {"bound": "hbm", "kernel": "the step's fused dequant + GEMV launches "
+                                                  "(dqg direct kernel), timed alone",
+                         "achieved": gemv.get("achieved_gbs"), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": gemv.get("frac"),
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy)",
-                         "kernel": "dqg::stream::gemv_stream_kernel (all 18 launches of a step)",
-                         "bytes_per_launch_avg": step_bytes // len(cs),
-                         "traffic": traffic},
-            "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
-                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                    "ms_per_step": round(e2e["ms"], 4),
-                    "path": "dequant_cuda.gemv (eager, pinned host x -> device -> pinned host y)"},
-            "gpu_launches": len(cs) * args.steps,
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-            "detail": detail,
-            "decode": decode,
-            "shape_sweep": shapes,
+                         "bytes_per_launch_avg": (gemv["bytes_per_step"] // gemv["launches"]
+                                                  if gemv else None),
+                         "us_per_launch": gemv.get("us_per_launch"),
+                         "traffic": load_traffic()},
+            "e2e": {"value": line["e2e"]["tokens_per_s"], "unit": UNIT,
+                    "h2d_bytes_per_step": line["e2e"]["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": line["e2e"]["d2h_bytes_per_step"],
+                    "ms_per_step": line["e2e"]["ms_per_token"],
+                    "path": "DecodeGraph: token ids from pinned host, graph replay, logits to "
+                            "pinned host, every step"},
+            "gpu_launches": decode_launches(D.LLAMA2_7B, world) * args.steps,
+            "clocks": clk.summary(t0, t1),
+            "cpu_baseline": (cpu_decode_baseline(args.cpu_seconds)
+                             if world == 1 and not args.no_cpu else None),
+            "decode": line,
+            **extra,
+            "gemv_sweep": sweep,
         }
-        print(json.dumps(line), flush=True)
-    del graph
+        print(json.dumps(out), flush=True)
     if dist is not None:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
+
+
+def decode_70b(args, dist, rank, world, dev):
+    """BASELINE config 5 at TP = world: Llama-3-70B architecture, INT4 g128
+    and INT2 g64, batch 1 and 8, 4096-token cache. Each format is packed once
+    per rank (PackedModel) and shared by the two batch sizes."""
+    import torch
+
+    from dequant_project_b200 import decode_bench
+    from dequant_project_b200 import decoder as D
+    from dequant_project_b200.packer import QuantConfig
+
+    out = {}
+    for bits, gs in ((4, 128), (2, 64)):
+        key = f"int{bits}_g{gs}"
+        try:
+            model = D.PackedModel.build(D.LLAMA3_70B, QuantConfig(bits, gs, False), seed=0,
+                                        device=dev)
+            for batch in (1, 8):
+                a = decode_bench.default_args(model="llama3-70b", bits=bits, group_size=gs,
+                                              batch=batch, kv_len=4096,
+                                              steps=max(10, args.steps // 10),
+                                              warmup=args.warmup)
+                a.packed_model = model
+                r = decode_bench.measure(a, dist, rank, world, dev, parts=False, e2e=False)
+                if r is not None:
+                    out[f"{key}_b{batch}"] = {k: r[k] for k in ("value", "unit", "tokens_per_s",
+                                                                "roofline", "bytes_per_rank")}
+            del model
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
+            out[key] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        torch.cuda.empty_cache()
+    return out if rank == 0 else None
 
 
 SHAPE_SWEEP = [(4096, 4096), (12288, 4096), (4096, 14336), (28672, 8192), (8192, 28672),
@@ -479,45 +523,94 @@ def cpu_baseline(cs, data, budget_s=10.0):
                               "sample": f"same sample, {passes1} passes in {el1:.1f} s"}}
 
 
+DECODE_SAMPLE_ROWS = 8   # rows of each matrix timed = N / DECODE_SAMPLE_ROWS
+
+
+def _decode_cpu_sample():
+    """One Llama-2-7B layer's linears (fused QKV, O, fused gate/up, down) and
+    the LM head, INT4 g128 asymmetric, each cut to its first N/8 rows and
+    packed by the numpy oracle: (name, rows, k, layers it stands for, x, qw, s, z)."""
+    import numpy as np
+
+    from oracle import packer_np as P
+
+    rng = np.random.default_rng(0)
+    out = []
+    for name, n, k, reps in (("qkv", 12288, 4096, 32), ("o", 4096, 4096, 32),
+                             ("gate_up", 22016, 4096, 32), ("down", 4096, 11008, 32),
+                             ("lm_head", 32000, 4096, 1)):
+        rows = n // DECODE_SAMPLE_ROWS
+        w = (rng.standard_normal((rows, k)) * 0.02).astype(np.float16)
+        qw, s, z = P.quantize_tensor(w, 4, 128, False, "sequential")
+        x = rng.standard_normal((1, k)).astype(np.float16)
+        out.append((name, rows, k, reps, x, qw, s, z))
+    return out
+
+
+def _time_decode_cpu(sample, threads):
+    """ms per token of the reference CPU path: every sampled GEMV once, scaled
+    by rows and by the layers it stands for."""
+    from oracle import native
+
+    ms = 0.0
+    for (_, rows, k, reps, x, qw, s, z) in sample:
+        t0 = time.perf_counter()
+        native.gemv(x, qw, s, z, 4, 128, False, False, threads=threads)
+        ms += (time.perf_counter() - t0) * 1e3 * DECODE_SAMPLE_ROWS * reps
+    return ms
+
+
+def cpu_decode_baseline(budget_s=10.0):
+    """The reference's CPU path (F.linear(x, packer.dequantize(W)) restated in
+    C, oracle/cpu_gemv.c) for the headline token, on this host's cores."""
+    from oracle import native
+
+    sample = _decode_cpu_sample()
+    threads = native.default_threads()
+    _time_decode_cpu(sample, threads)
+    samples, t0 = [], time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or len(samples) < 3:
+        samples.append(_time_decode_cpu(sample, threads))
+    ms = statistics.median(samples)
+    return {"value": round(1000.0 / ms, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "ms_per_token": round(ms, 1),
+            "sample": f"one layer's linears (QKV, O, gate/up, down) and the LM head of the "
+                      f"headline model, INT4 g128, first N/{DECODE_SAMPLE_ROWS} rows of each, "
+                      f"scaled by rows and by 32 layers; attention and norms (<1% of the CPU "
+                      f"time) left out; median of {len(samples)} passes in "
+                      f"{time.perf_counter() - t0:.1f} s; C restatement of "
+                      f"F.linear(x, packer.dequantize(pw)), OpenMP, {threads} threads"}
+
+
 def run_reference(args, rank, world):
-    """The reference CPU path (oracle port), rank 0 only; other ranks exit 0."""
+    """The reference CPU path (oracle port) for the headline token, rank 0
+    only; other ranks exit 0."""
     if rank != 0:
         return
     from oracle import native
 
-    cs = cases()
-    sample = cpu_cases_sample(cs, None)
+    sample = _decode_cpu_sample()
     threads = native.default_threads()
-    from oracle import native as _n
-    _n.lib()
-    step_bytes = sum(case_bytes(ns, k, bits, gs, sym, m)
-                     for (ns, k, bits, gs, sym, m, *_r) in sample)
-
-    def step():
-        for (ns, k, bits, gs, sym, m, _, x, qw, s, z) in sample:
-            native.gemv(x, qw, s, z, bits, gs or k, sym, False, threads=threads)
-
     for _ in range(max(3, args.warmup)):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    el = time.perf_counter() - t0
-    ms = el / args.steps * 1e3
-    value = step_bytes / (ms * 1e-3) / 1e9
+        _time_decode_cpu(sample, threads)
+    steps = max(3, min(args.steps, 20))
+    ms = statistics.median(_time_decode_cpu(sample, threads) for _ in range(steps))
+    value = 1000.0 / ms
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp16 activations x int2/4/8 codes, fp32 accumulate",
-        "data": "synthetic (random-init N(0,0.02) weights, N(0,1) activations)",
-        "config": workload_config(1), "impl": "reference",
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp16 activations x int4 codes, fp32 accumulate",
+        "data": "synthetic (random-init N(0,0.02) weights)",
+        "config": workload_config(world), "impl": "reference",
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
                          "kind": "port",
-                         "sample": "each step: the 18 sweep cases on the first N/8 rows of each "
-                                   "weight; C restatement of F.linear(x, packer.dequantize(pw)) "
-                                   f"(oracle/cpu_gemv.c), OpenMP, {threads} threads"},
-        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                         "sample": "each step: one layer's linears and the LM head, first "
+                                   f"N/{DECODE_SAMPLE_ROWS} rows of each, scaled to the "
+                                   "32-layer token; C restatement of F.linear(x, "
+                                   "packer.dequantize(pw)) (oracle/cpu_gemv.c), OpenMP, "
+                                   f"{threads} threads"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -526,14 +619,17 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-detail", action="store_true", help="skip the per-case table")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-decode", action="store_true",
-                    help="skip the decoder ms/token measurement")
+                    help="skip the batch-8 and 70B decoder sub-measurements")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the GEMV sweep (N=1)")
+    ap.add_argument("--with-70b", action="store_true",
+                    help="also run BASELINE config 5 (70B) at N=1")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

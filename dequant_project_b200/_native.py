@@ -47,9 +47,26 @@ def lib() -> ctypes.CDLL:
     h.dqg_silu_mul.argtypes = [vp, vp, i64, i64, vp]
     h.dqg_set_weight_prefetch.restype = i32
     h.dqg_set_weight_prefetch.argtypes = [i32]
+    h.dqg_set_gemv_path.restype = i32
+    h.dqg_set_gemv_path.argtypes = [i32]
     h.dqg_debug_gemv_starved.restype = i32
     h.dqg_debug_gemv_starved.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32,
                                          ctypes.c_uint64, vp]
+    u64p = ctypes.POINTER(ctypes.c_uint64)
+    h.dqg_ipc_export.restype = i32
+    h.dqg_ipc_export.argtypes = [vp, vp, u64p]
+    h.dqg_ipc_open.restype = i32
+    h.dqg_ipc_open.argtypes = [vp, ctypes.POINTER(ctypes.c_void_p)]
+    h.dqg_ipc_close.restype = i32
+    h.dqg_ipc_close.argtypes = [vp]
+    h.dqg_peer_allreduce.restype = i32
+    h.dqg_peer_allreduce.argtypes = [vp, vp, i64, u64p, u64p, vp, i64, i32, i32,
+                                     ctypes.c_uint64, vp]
+    h.dqg_decode_attention_workspace.restype = i32
+    h.dqg_decode_attention_workspace.argtypes = [i64, i64, i64, i64, u64p]
+    h.dqg_decode_attention.restype = i32
+    h.dqg_decode_attention.argtypes = [vp, vp, vp, vp, vp, ctypes.c_uint64, i64, i64, i64, i64,
+                                       i64, i64, vp]
     h.dqg_stream_plan.restype = i32
     h.dqg_stream_plan.argtypes = [i64, i64, i64, i64, i64, i32, ctypes.POINTER(ctypes.c_int32), i32]
     _lib = h
@@ -59,7 +76,9 @@ def lib() -> ctypes.CDLL:
 # Every symbol the C header declares; tests check the library exports them all.
 EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_dequantize",
             "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul",
-            "dqg_stream_plan", "dqg_set_weight_prefetch", "dqg_debug_gemv_starved")
+            "dqg_stream_plan", "dqg_set_weight_prefetch", "dqg_debug_gemv_starved",
+            "dqg_set_gemv_path", "dqg_decode_attention_workspace", "dqg_decode_attention",
+            "dqg_ipc_export", "dqg_ipc_open", "dqg_ipc_close", "dqg_peer_allreduce")
 
 
 def check(rc: int) -> None:

@@ -4,11 +4,13 @@
 // :310-317 dequantize, :339-361 gemv, kernels/smoke.cu:15-25 add_one) with the
 // same messages, adapted to raw pointers: dtype/contiguity checks become
 // pointer-kind and alignment checks. Nothing here allocates or synchronises.
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/dequant_b200.h"
@@ -89,6 +91,35 @@ bool cached_stream_plan(int M, int N, int K, int bits, int group_size, int sms,
   if (e.ok) *out = e.plan;
   return e.ok;
 }
+
+// Direct-kernel plans of recent call shapes (same scheme as above).
+struct DirectEntry {
+  int M, N, K, bits, group_size, sms;
+  bool ok;
+  dqg::DirectPlan plan;
+  bool used;
+};
+
+bool cached_direct_plan(int M, int N, int K, int bits, int group_size, int sms,
+                        dqg::DirectPlan* out) {
+  thread_local DirectEntry cache[32] = {};
+  const uint32_t h = (static_cast<uint32_t>(M) * 2654435761u) ^ (static_cast<uint32_t>(N) * 40503u) ^
+                     (static_cast<uint32_t>(K) * 2246822519u) ^ static_cast<uint32_t>(bits << 3) ^
+                     static_cast<uint32_t>(group_size) * 3266489917u ^ static_cast<uint32_t>(sms);
+  DirectEntry& e = cache[(h ^ (h >> 15)) & 31];
+  if (!(e.used && e.M == M && e.N == N && e.K == K && e.bits == bits &&
+        e.group_size == group_size && e.sms == sms)) {
+    e.ok = dqg::plan_direct(M, N, K, bits, group_size, sms, &e.plan);
+    e.M = M; e.N = N; e.K = K; e.bits = bits; e.group_size = group_size; e.sms = sms;
+    e.used = true;
+  }
+  if (e.ok) *out = e.plan;
+  return e.ok;
+}
+
+// 0: pick the kernel per shape (direct, else streaming, else general);
+// 1: never the direct kernel (tests and comparisons).
+std::atomic<int> g_gemv_path{0};
 
 int sm_count(int dev) {
   static int cache[64] = {0};
@@ -218,8 +249,20 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   a.group_size = static_cast<int>(group_size);
   a.symmetric = symmetric != 0;
   a.interleaved = interleaved != 0;
-  // The streaming kernel whenever its plan fits (activations resident in
-  // shared memory, 16-byte-aligned scales/zeros); the general kernel otherwise.
+  // The direct kernel for group-wise formats whose group is one MMA step and
+  // whose activations fit one CTA; else the streaming kernel whenever its
+  // plan fits (activations resident per CTA or per split-K cluster,
+  // 16-byte-aligned scales/zeros); the general kernel otherwise.
+  if (g_gemv_path.load() == 0) {
+    dqg::DirectPlan dplan;
+    if (cached_direct_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                           static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
+                           &dplan)) {
+      e = dqg::launch_direct(a, dplan, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+      return ok();
+    }
+  }
   dqg::StreamPlan splan;
   const bool meta_aligned = reinterpret_cast<uintptr_t>(scales) % 16 == 0 &&
                             (zeros == nullptr || reinterpret_cast<uintptr_t>(zeros) % 16 == 0);
@@ -373,6 +416,80 @@ int dqg_stream_plan(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group
   return ok();
 }
 
+int dqg_decode_attention_workspace(int64_t M, int64_t n_q_heads, int64_t n_kv_heads,
+                                   int64_t T, uint64_t* bytes) {
+  if (bytes == nullptr) return fail(DQG_ERR_INVALID, "bytes must not be null");
+  if (M < 1 || M > 65535 || n_kv_heads < 1 || n_q_heads < n_kv_heads ||
+      n_q_heads % n_kv_heads != 0 || n_q_heads / n_kv_heads > 16 || n_q_heads > 65535)
+    return fail(DQG_ERR_INVALID,
+                "head counts (%lld query, %lld KV) must give 1..16 query heads per KV head",
+                (long long)n_q_heads, (long long)n_kv_heads);
+  if (T < 1 || T > (1 << 24)) return fail(DQG_ERR_INVALID, "T=%lld out of range", (long long)T);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  *bytes = dqg::attention_workspace_bytes(static_cast<int>(M), static_cast<int>(n_q_heads),
+                                          static_cast<int>(n_kv_heads), static_cast<int>(T),
+                                          sm_count(dev));
+  return ok();
+}
+
+int dqg_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                         void* workspace, uint64_t workspace_bytes, int64_t M, int64_t n_q_heads,
+                         int64_t n_kv_heads, int64_t head_dim, int64_t T, int64_t capacity,
+                         void* stream) {
+  if (head_dim != 128)
+    return fail(DQG_ERR_UNSUPPORTED, "decode attention handles head_dim 128, got %lld",
+                (long long)head_dim);
+  uint64_t need = 0;
+  int rc = dqg_decode_attention_workspace(M, n_q_heads, n_kv_heads, T, &need);
+  if (rc) return rc;
+  if (capacity < T)
+    return fail(DQG_ERR_INVALID, "T=%lld positions exceed the cache capacity %lld", (long long)T,
+                (long long)capacity);
+  if (M * n_kv_heads * capacity * head_dim > (int64_t(1) << 40))
+    return fail(DQG_ERR_INVALID, "cache too large");
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(DQG_ERR_INVALID, "workspace of %llu bytes needed, %llu given",
+                (unsigned long long)need, (unsigned long long)workspace_bytes);
+  const void* ptrs[5] = {q, k_cache, v_cache, out, workspace};
+  const char* names[5] = {"q", "k_cache", "v_cache", "out", "workspace"};
+  for (int i = 0; i < 5; ++i) {
+    if (ptrs[i] == nullptr) return fail(DQG_ERR_INVALID, "%s must not be null", names[i]);
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16)
+      return fail(DQG_ERR_INVALID, "%s must be 16-byte aligned", names[i]);
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  dqg::AttnParams p;
+  p.q = static_cast<const __half*>(q);
+  p.kc = static_cast<const __half*>(k_cache);
+  p.vc = static_cast<const __half*>(v_cache);
+  p.o = static_cast<__half*>(out);
+  p.M = static_cast<int>(M);
+  p.Hq = static_cast<int>(n_q_heads);
+  p.Hkv = static_cast<int>(n_kv_heads);
+  p.g = p.Hq / p.Hkv;
+  p.cap = static_cast<int>(capacity);
+  p.T = static_cast<int>(T);
+  p.S = dqg::attention_splits(p.M, p.Hkv, p.T, sm_count(dev), &p.Ts);
+  const size_t mh = static_cast<size_t>(M) * n_kv_heads;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.part = reinterpret_cast<float*>(ws);
+  p.ml = reinterpret_cast<float*>(ws + mh * p.S * p.g * 128 * 4);
+  p.tickets = reinterpret_cast<unsigned*>(ws + mh * p.S * p.g * 128 * 4 + mh * p.S * p.g * 2 * 4);
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / 11.313708498984761);  // log2(e)/sqrt(128)
+  e = dqg::launch_decode_attention(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
+  return ok();
+}
+
+int dqg_set_gemv_path(int path) {
+  if (path != 0 && path != 1) return -1;
+  return g_gemv_path.exchange(path);
+}
+
 int dqg_set_weight_prefetch(int enable) {
   const int prev = dqg::weight_prefetch() ? 1 : 0;
   dqg::set_weight_prefetch(enable != 0);
@@ -419,6 +536,88 @@ int dqg_debug_gemv_starved(const int32_t* qweight, const void* scales, const voi
   a.interleaved = interleaved != 0;
   e = dqg::launch_stream(a, splan, static_cast<cudaStream_t>(stream), wait_ns, true);
   if (e != cudaSuccess) return cuda_fail(e, "starved gemv launch");
+  return ok();
+}
+
+int dqg_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr)
+    return fail(DQG_ERR_INVALID, "ptr, handle and offset must not be null");
+  // Base of the allocation that holds ptr (the IPC handle names the whole
+  // allocation); the driver function is looked up at run time so that the
+  // library does not link the driver.
+  using AddrRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddrRange range_fn = nullptr;
+  if (range_fn == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return fail(DQG_ERR_CUDA, "cuMemGetAddressRange is not available");
+    range_fn = reinterpret_cast<AddrRange>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(DQG_ERR_INVALID, "ptr is not device memory of this process");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(ptr) - base);
+  return ok();
+}
+
+int dqg_ipc_open(const void* handle, void** base) {
+  if (handle == nullptr || base == nullptr)
+    return fail(DQG_ERR_INVALID, "handle and base must not be null");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return ok();
+}
+
+int dqg_ipc_close(void* base) {
+  if (base == nullptr) return fail(DQG_ERR_INVALID, "base must not be null");
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return ok();
+}
+
+int dqg_peer_allreduce(const void* in, void* out, int64_t n, const uint64_t* peer_data,
+                       const uint64_t* peer_flags, uint32_t* ctl, int64_t cap, int rank,
+                       int world, uint64_t wait_ns, void* stream) {
+  if (world < 1 || world > dqg::kArMaxRanks || rank < 0 || rank >= world)
+    return fail(DQG_ERR_INVALID, "rank %d / world %d out of range (at most %d ranks)", rank, world,
+                dqg::kArMaxRanks);
+  if (n < 8 || n % 8 != 0 || n > cap)
+    return fail(DQG_ERR_INVALID, "n=%lld must be a positive multiple of 8 and at most cap=%lld",
+                (long long)n, (long long)cap);
+  if (cap % 8 != 0) return fail(DQG_ERR_INVALID, "cap must be a multiple of 8");
+  if (in == nullptr || out == nullptr || peer_data == nullptr || peer_flags == nullptr ||
+      ctl == nullptr)
+    return fail(DQG_ERR_INVALID, "pointers must not be null");
+  if (reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(DQG_ERR_INVALID, "in and out must be 16-byte aligned");
+  if (wait_ns != 0 && (wait_ns < 1000000ull || wait_ns > 10000000000ull))
+    return fail(DQG_ERR_INVALID, "wait_ns must be 0 (default) or in [1 ms, 10 s]");
+  dqg::PeerReduceParams p = {};
+  p.in = static_cast<const __half*>(in);
+  p.out = static_cast<__half*>(out);
+  p.n = n;
+  p.cap = cap;
+  for (int r = 0; r < world; ++r) {
+    if (peer_data[r] == 0 || peer_flags[r] == 0 || peer_data[r] % 16)
+      return fail(DQG_ERR_INVALID, "peer buffers of rank %d missing or misaligned", r);
+    p.peer_data[r] = peer_data[r];
+    p.peer_flags[r] = peer_flags[r];
+  }
+  p.ctl = ctl;
+  p.rank = rank;
+  p.world = world;
+  p.wait_ns = wait_ns ? wait_ns : 2000000000ull;
+  cudaError_t e = dqg::launch_peer_allreduce(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "peer_allreduce launch");
   return ok();
 }
 

@@ -635,7 +635,8 @@ cudaError_t read_device_status(int device, uint32_t* status, bool reset) {
   if (e != cudaSuccess) return e;
   if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
   cudaError_t (*readers[])(uint32_t*, bool) = {read_status_gemv, read_status_stream_b2,
-                                                read_status_stream_b4, read_status_stream_b8};
+                                                read_status_stream_b4, read_status_stream_b8,
+                                                read_status_peer};
   *status = 0;
   for (auto rd : readers) {
     uint32_t v = 0;

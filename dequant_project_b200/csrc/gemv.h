@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace dqg {
@@ -80,6 +81,16 @@ cudaError_t launch_gemv(const GemvArgs& args, const GemvPlan& plan, cudaStream_t
 #define DQG_STREAM_NCW 8
 #endif
 constexpr int kStreamNCW = DQG_STREAM_NCW;  // consumer (tensor-core) warps
+#ifndef DQG_STREAM_SMEM
+#define DQG_STREAM_SMEM 232448
+#endif
+#ifndef DQG_STREAM_MIN_BLOCKS
+#define DQG_STREAM_MIN_BLOCKS 1
+#endif
+// Shared memory a streaming CTA may use, and CTAs per SM the register budget
+// is sized for.
+constexpr int kStreamSmemBytes = DQG_STREAM_SMEM;
+constexpr int kStreamMinBlocks = DQG_STREAM_MIN_BLOCKS;
 constexpr int kStreamThreads = 32 * (2 + kStreamNCW);  // + producer + reducer
 constexpr int kStreamNRB = 4;     // tile reduction buffers
 constexpr int kStreamXMaxBytes = 100 * 1024;   // cap on resident activations (per CTA)
@@ -118,6 +129,57 @@ struct StreamPlan {
 
 bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, StreamPlan* plan);
 
+// ------------------------------------------------------------------ direct
+// Direct kernel (gemv_direct.cuh): group-wise formats with one MMA step per
+// group, activations resident in one CTA; every warp streams its own range of
+// work units from global memory into registers.
+#ifndef DQG_DIRECT_NW
+#define DQG_DIRECT_NW 8
+#endif
+#ifndef DQG_DIRECT_RING
+#define DQG_DIRECT_RING 8192
+#endif
+constexpr int kDirectNW = DQG_DIRECT_NW;         // warps per CTA
+constexpr int kDirectThreads = 32 * kDirectNW;
+constexpr int kDirectRingBytes = DQG_DIRECT_RING;  // per-warp ring of packed words in flight
+constexpr int kDirectMaxSmem = 232448;
+
+struct DirectParams {
+  const uint16_t* x;
+  const uint32_t* qw;
+  const uint16_t* scales;
+  const uint16_t* zeros;
+  uint16_t* y;
+  int M, N, K, G;
+  int Gp;                 // groups per tile padded to whole units
+  int xp;                 // bytes per permuted activation row in shared memory
+  int off_x, off_sx, off_zero, off_red, off_tiles, off_ring;
+  int prefetch;           // 1: first ring issued before the dependent-launch wait
+};
+
+struct DirectPlan {
+  int wpl, mp, gs, Gp, xp, off_x, off_sx, off_zero, off_red, off_tiles, off_ring, smem, grid;
+};
+
+bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, DirectPlan* plan);
+cudaError_t launch_direct(const GemvArgs& args, const DirectPlan& plan, cudaStream_t stream);
+
+// ------------------------------------------------------- decode attention
+struct AttnParams {
+  const __half* q;        // [M, Hq, 128]
+  const __half* kc;       // [M, Hkv, cap, 128]
+  const __half* vc;
+  __half* o;              // [M, Hq, 128]
+  float* part;            // workspace: [M * Hkv][S][g][128] partial outputs
+  float* ml;              // workspace: [M * Hkv][S][g][2] running max and sum
+  unsigned* tickets;      // workspace: [M * Hkv] split counters (zero between calls)
+  int M, Hq, Hkv, g, cap, T, S, Ts;
+  float scale_log2;       // log2(e) / sqrt(128)
+};
+int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out);
+size_t attention_workspace_bytes(int M, int Hq, int Hkv, int T, int num_sms);
+cudaError_t launch_decode_attention(const AttnParams& p, cudaStream_t stream);
+
 // Process-wide switch (default on): the streaming kernel issues its first
 // weight ring before waiting for the previous grid on the stream.
 void set_weight_prefetch(bool on);
@@ -146,6 +208,26 @@ cudaError_t read_status_gemv(uint32_t* status, bool reset);
 cudaError_t read_status_stream_b2(uint32_t* status, bool reset);
 cudaError_t read_status_stream_b4(uint32_t* status, bool reset);
 cudaError_t read_status_stream_b8(uint32_t* status, bool reset);
+cudaError_t read_status_peer(uint32_t* status, bool reset);
+
+// ------------------------------------------------------- peer all-reduce
+// One-shot all-reduce of fp16 tensors over peer memory (peer_reduce.cu).
+constexpr int kArChunk = 2048;    // elements per CTA (one flag per chunk and rank)
+constexpr int kArMaxRanks = 8;
+
+struct PeerReduceParams {
+  const __half* in;
+  __half* out;
+  long long n;                    // elements, a multiple of 8
+  long long cap;                  // elements per parity half of each exchange buffer
+  unsigned long long peer_data[kArMaxRanks];   // each rank's exchange buffer (2 * cap fp16)
+  unsigned long long peer_flags[kArMaxRanks];  // each rank's flags [chunks][world] u32
+  uint32_t* ctl;                  // this rank's [epoch, ticket]
+  int rank, world;
+  unsigned long long wait_ns;
+};
+
+cudaError_t launch_peer_allreduce(const PeerReduceParams& p, cudaStream_t stream);
 
 cudaError_t launch_add_one(const float* x, float* out, int64_t n, cudaStream_t stream);
 

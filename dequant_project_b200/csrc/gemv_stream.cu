@@ -73,7 +73,7 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
                      round_up(M * (grouped ? KC / group_size : 1) * 4, 128) +
                      (C > 1 ? round_up(kStreamNRB * C * kTile * M * 4, 128) : 0) + red_bytes +
                      kStreamBarBytes + 640 + 2 * meta_stride + 2 * stage_bytes_for(KC);
-    if ((C - 1) * KC < K && xb <= kStreamXMaxBytes && need <= kMaxSmemBytes) break;
+    if ((C - 1) * KC < K && xb <= kStreamXMaxBytes && need <= kStreamSmemBytes) break;
     C *= 2;
     if (C > kStreamMaxCluster || C > num_sms) return false;
   }
@@ -114,12 +114,12 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
   pl.stage_bytes = round_up(kTile * pl.w_pitch, 128);
   // Ring stages with two metadata buffers first; then more metadata buffers
   // (one per tile the ring can hold, plus one) while they fit.
-  int stages = (kMaxSmemBytes - off - 2 * pl.meta_stride) / pl.stage_bytes;
+  int stages = (kStreamSmemBytes - off - 2 * pl.meta_stride) / pl.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
   int n_meta = (stages + n_slabs - 1) / n_slabs + 1;
   if (n_meta > kStreamMaxMeta) n_meta = kStreamMaxMeta;
-  while (n_meta > 2 && off + n_meta * pl.meta_stride + stages * pl.stage_bytes > kMaxSmemBytes)
+  while (n_meta > 2 && off + n_meta * pl.meta_stride + stages * pl.stage_bytes > kStreamSmemBytes)
     --n_meta;
   if (n_meta < 2) n_meta = 2;
   pl.stages = stages;

@@ -248,7 +248,7 @@ __device__ __forceinline__ void combine(const float (&D)[NCH][4], float* P) {
 }
 
 template <int BITS, bool SYM, bool INTER, int WPL, int GS>
-__global__ void __launch_bounds__(kStreamThreads, 1)
+__global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks)
     gemv_stream_kernel(const __grid_constant__ StreamParams p) {
   constexpr bool GROUPED = GS > 0;
   constexpr int MP = GROUPED ? 8 / GS : 8;  // activation-row columns per group slot
@@ -828,6 +828,10 @@ cudaError_t launch_one(const StreamParams& p, int grid, int smem, cudaStream_t s
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmemBytes);
+    if (e != cudaSuccess) return e;
+    // The whole carveout as shared memory, for every variant alike, so that a
+    // CTA of the next launch can become resident beside one of this launch.
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }

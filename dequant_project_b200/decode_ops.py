@@ -10,6 +10,8 @@ tensor.
 
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.nn.functional as F
 
@@ -85,4 +87,46 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     out = torch.empty((m, i), dtype=torch.float16, device=gate_up.device)
     _native.check(_native.lib().dqg_silu_mul(gate_up.data_ptr(), out.data_ptr(), m, i,
                                              _stream(gate_up)))
+    return out
+
+
+def attention_workspace(m: int, n_q_heads: int, n_kv_heads: int, max_positions: int,
+                        device) -> torch.Tensor:
+    """Zeroed workspace for ``attention`` calls of up to ``max_positions``
+    positions (the library keeps its split counters at zero afterwards)."""
+    import ctypes
+    n = ctypes.c_uint64(0)
+    _native.check(_native.lib().dqg_decode_attention_workspace(
+        m, n_q_heads, n_kv_heads, max_positions, ctypes.byref(n)))
+    return torch.zeros(max(int(n.value), 16), dtype=torch.uint8, device=device)
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, positions: int,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One query per sequence and head over cache positions 0..positions-1.
+
+    q [M, Hq, D] fp16; k_cache, v_cache [M, Hkv, capacity, D] fp16 (query
+    heads grouped consecutively per KV head). Returns [M, Hq, D] fp16. CUDA
+    tensors go through ``dqg_decode_attention`` (D = 128; ``workspace`` from
+    ``attention_workspace``); CPU tensors take an fp32 softmax(q k^T /
+    sqrt(D)) v in torch (the CPU tests' stand-in)."""
+    m, hq, d = q.shape
+    hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    if not q.is_cuda:
+        g = hq // hkv
+        qf = q.float().view(m, hkv, g, d)
+        kc = k_cache[:, :, :positions].float()
+        vc = v_cache[:, :, :positions].float()
+        s = torch.einsum("mkgd,mktd->mkgt", qf, kc) / math.sqrt(d)
+        p = torch.softmax(s, dim=-1)
+        return torch.einsum("mkgt,mktd->mkgd", p, vc).reshape(m, hq, d).to(torch.float16)
+    for t in (q, k_cache, v_cache):
+        if t.dtype != torch.float16 or not t.is_contiguous():
+            raise RuntimeError("attention takes contiguous float16 tensors")
+    if workspace is None:
+        workspace = attention_workspace(m, hq, hkv, positions, q.device)
+    out = torch.empty_like(q)
+    _native.check(_native.lib().dqg_decode_attention(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+        workspace.data_ptr(), workspace.numel(), m, hq, hkv, d, positions, cap, _stream(q)))
     return out

@@ -31,7 +31,6 @@ collectives included) for timing; eager ``step`` takes any position.
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 from typing import Callable
 
@@ -84,25 +83,6 @@ def rope_tables(head_dim: int, theta: float, positions: int, device) -> tuple:
     ang = torch.arange(positions, dtype=torch.float64, device=device)[:, None] * inv[None, :]
     ang = torch.cat([ang, ang], dim=-1)
     return ang.cos().float(), ang.sin().float()
-
-
-def attention(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor) -> torch.Tensor:
-    """One query per sequence and head over the cache.
-
-    q [M, Hq, D] fp16; kc, vc [M, Hkv, T, D] fp16 (T = positions to attend).
-    Returns [M, Hq, D] fp16. On the GPU this is torch's fused
-    scaled-dot-product attention (grouped KV heads); elsewhere an fp32
-    softmax(q k^T / sqrt(D)) v."""
-    m, hq, d = q.shape
-    hkv = kc.shape[1]
-    if q.is_cuda:
-        o = F.scaled_dot_product_attention(q.unsqueeze(2), kc, vc, enable_gqa=hq != hkv)
-        return o.squeeze(2)
-    g = hq // hkv
-    qf = q.float().view(m, hkv, g, d)
-    s = torch.einsum("mkgd,mktd->mkgt", qf, kc.float()) / math.sqrt(d)
-    p = torch.softmax(s, dim=-1)
-    return torch.einsum("mkgt,mktd->mkgd", p, vc.float()).reshape(m, hq, d).to(torch.float16)
 
 
 def _default_linear(x: torch.Tensor, pw: PackedWeight) -> torch.Tensor:
@@ -223,12 +203,16 @@ class TPDecoder:
     matrices come from: ``None`` draws them from ``seed`` and quantizes them
     (``SeededWeights``); a ``PackedModel`` (``PackedModel.load`` reads one
     from disk) supplies them already packed, so no rank quantizes anything.
-    Each rank takes its shard of every full matrix."""
+    Each rank takes its shard of every full matrix. ``allreduce`` picks the
+    collective after the row-parallel layers on CUDA ranks: ``"peer"`` (the
+    one-shot all-reduce over peer memory of ``peer_reduce``, the default) or
+    ``"nccl"`` (``torch.distributed.all_reduce``); CPU ranks always use the
+    process group. ``close()`` releases the peer mappings."""
 
     def __init__(self, cfg: DecoderConfig, qcfg: QuantConfig, *, world: int = 1, rank: int = 0,
                  group=None, device=None, seed: int = 0, batch: int = 1, kv_len: int = 2048,
                  max_new: int = 1, quantize_lm_head: bool = True,
-                 linear_fn: Callable | None = None, weights=None):
+                 linear_fn: Callable | None = None, weights=None, allreduce: str = "peer"):
         if cfg.n_heads % world or cfg.n_kv_heads % world:
             raise ValueError(f"{cfg.n_heads} query / {cfg.n_kv_heads} KV heads do not split "
                              f"over {world} ranks")
@@ -303,6 +287,22 @@ class TPDecoder:
         self.final_norm = ones
         self.cos, self.sin = rope_tables(d, cfg.rope_theta, self.capacity, self.device)
         self.reset_cache(seed)
+        self._attn_ws = (ops.attention_workspace(batch, self.hq, self.hkv, self.capacity,
+                                                 self.device)
+                         if self.device.type == "cuda" else None)
+        if allreduce not in ("peer", "nccl"):
+            raise ValueError(f"allreduce must be 'peer' or 'nccl', got {allreduce!r}")
+        self._peer = None
+        if world > 1 and allreduce == "peer" and self.device.type == "cuda":
+            from dequant_project_b200.peer_reduce import PeerAllReduce
+            self._peer = PeerAllReduce(group, self.device, batch * cfg.hidden)
+
+    def close(self) -> None:
+        """Release the peer all-reduce's mappings (before the process group
+        is destroyed); the decoder then uses the process group's all-reduce."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     # ------------------------------------------------------------------ cache
     def reset_cache(self, seed: int = 0) -> None:
@@ -325,6 +325,8 @@ class TPDecoder:
 
     # -------------------------------------------------------------- forward
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self._peer is not None:
+            return self._peer(t)
         if self.world > 1:
             import torch.distributed as dist
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
@@ -359,7 +361,7 @@ class TPDecoder:
             qkv = self._linear(x, w["qkv"])
             kc, vc = self.k_cache[layer], self.v_cache[layer]
             q = ops.rope_kv_append(qkv, cos, sin, kc, vc, pos, self.hq, self.hkv)
-            a = attention(q, kc[:, :, :pos + 1], vc[:, :, :pos + 1])
+            a = ops.attention(q, kc, vc, pos + 1, self._attn_ws)
             o = self._all_reduce(self._linear(a.reshape(m, nq), w["o"]))
             x = ops.add_rms_norm(h, o, self.mlp_norm[layer], cfg.eps)
             act = ops.silu_mul(self._linear(x, w["gu"]))

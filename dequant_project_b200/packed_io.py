@@ -67,7 +67,9 @@ def load_packed(path, device=None) -> tuple[dict[str, PackedWeight], dict, dict]
     """Read a file written by ``save_packed``: (packed weights, tensors, meta),
     moved to ``device`` when given. Raises ValueError for another format or a
     record whose tensors do not match its descriptor."""
-    blob = torch.load(Path(path), map_location="cpu", weights_only=True)
+    # Memory-mapped: tensors left on the host stay backed by the file, so
+    # several processes loading one model share its pages.
+    blob = torch.load(Path(path), map_location="cpu", weights_only=True, mmap=True)
     if not isinstance(blob, dict) or blob.get("format") != FORMAT:
         raise ValueError(f"{path} is not a {FORMAT} file")
     if int(blob.get("version", -1)) != VERSION:

@@ -1,0 +1,128 @@
+"""One-shot all-reduce over NVLink peer memory for the tensor-parallel decoder.
+
+The decoder's row-parallel layers (O and down projections) end in an
+all-reduce of a few KB to a few hundred KB of fp16 partial outputs, two per
+layer (the reference's ``dequant/byte_model.py:179-251`` counts these bytes;
+the reference itself has no multi-GPU code). At these
+sizes a collective is bound by latency, not bandwidth, so this replaces NCCL's
+algorithms with one exchange round through memory every rank can address:
+
+* at set-up, each rank allocates one exchange buffer (two parity halves of
+  ``cap`` fp16 values plus a flag array) and a two-word call counter, zeroed;
+  the buffers' CUDA IPC handles are swapped over the process group
+  (``all_gather_object``) and every peer's buffer is mapped into this process;
+* each call (``dqg_peer_allreduce`` in libdequant_b200.so) copies the input
+  into this rank's buffer, raises a flag in every peer's flag array, waits
+  (bounded) for every peer's flag and sums all ranks' buffers in rank order in
+  fp32 with one rounding, so every rank gets the same bits.
+
+The call counter lives on the device, so calls can be captured in a CUDA graph
+and replayed. All ranks must make the same sequence of calls, as with any
+collective. ``close()`` unmaps the peers' buffers; call it (or let the decoder
+call it) before the process group is destroyed.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from dequant_project_b200 import _native
+
+CHUNK = 2048          # elements per CTA of the kernel (one flag per chunk and rank)
+MAX_RANKS = 8
+HANDLE_BYTES = 64     # sizeof(cudaIpcMemHandle_t)
+
+
+class CudaIpc:
+    """CUDA IPC of device memory through the library's C ABI."""
+
+    def export(self, ptr: int) -> tuple[bytes, int]:
+        buf = ctypes.create_string_buffer(HANDLE_BYTES)
+        off = ctypes.c_uint64(0)
+        _native.check(_native.lib().dqg_ipc_export(ptr, buf, ctypes.byref(off)))
+        return buf.raw, off.value
+
+    def open(self, handle: bytes) -> int:
+        base = ctypes.c_void_p(0)
+        _native.check(_native.lib().dqg_ipc_open(handle, ctypes.byref(base)))
+        return base.value
+
+    def close(self, base: int) -> None:
+        _native.check(_native.lib().dqg_ipc_close(base))
+
+
+def _round_up(v: int, m: int) -> int:
+    return (v + m - 1) // m * m
+
+
+class PeerAllReduce:
+    """Sum-all-reduce of fp16 tensors of at most ``max_elems`` values across
+    the ranks of ``group`` (one process per GPU of one node, at most 8).
+
+    ``ipc`` maps buffers between processes (``CudaIpc`` by default; the CPU
+    tests pass a stand-in to check the exchange). ``wait_ns`` bounds each wait
+    for a peer (0: the library's 2 s)."""
+
+    def __init__(self, group, device, max_elems: int, wait_ns: int = 0, ipc=None):
+        import torch.distributed as dist
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 1 <= self.world <= MAX_RANKS:
+            raise ValueError(f"peer all-reduce takes 1..{MAX_RANKS} ranks, got {self.world}")
+        if max_elems < 8:
+            raise ValueError("max_elems must be at least 8")
+        self.device = torch.device(device)
+        self.cap = _round_up(max_elems, 8)
+        self.chunks = (self.cap + CHUNK - 1) // CHUNK
+        self.wait_ns = int(wait_ns)
+        self._ipc = ipc if ipc is not None else CudaIpc()
+        data_bytes = 2 * self.cap * 2
+        flag_bytes = self.chunks * self.world * 4
+        # One allocation: [exchange data | flags], so one handle per rank.
+        self.buffer = torch.zeros(data_bytes + flag_bytes, dtype=torch.uint8, device=self.device)
+        self.ctl = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._flag_off = data_bytes
+        handle, offset = self._ipc.export(self.buffer.data_ptr())
+        infos = [None] * self.world
+        dist.all_gather_object(infos, (self.rank, handle, offset), group=group)
+        self._opened: list[int] = []
+        data_ptrs = []
+        for r, (rr, h, off) in enumerate(infos):
+            if rr != r:
+                raise RuntimeError(f"peer exchange out of order: slot {r} holds rank {rr}")
+            if r == self.rank:
+                data_ptrs.append(self.buffer.data_ptr())
+            else:
+                base = self._ipc.open(h)
+                self._opened.append(base)
+                data_ptrs.append(base + off)
+        self.peer_data = (ctypes.c_uint64 * self.world)(*data_ptrs)
+        self.peer_flags = (ctypes.c_uint64 * self.world)(*[p + self._flag_off for p in data_ptrs])
+        # No rank may raise a flag in a buffer its peer has not mapped yet.
+        dist.barrier(group=group)
+
+    def __call__(self, t: torch.Tensor) -> torch.Tensor:
+        """In-place sum over ranks of the contiguous fp16 tensor ``t``."""
+        if self._opened is None:
+            raise RuntimeError("peer all-reduce used after close()")
+        if t.dtype != torch.float16 or not t.is_contiguous() or t.device != self.device:
+            raise RuntimeError("peer all-reduce takes a contiguous float16 tensor on its device")
+        n = t.numel()
+        if n % 8 or n > self.cap or n == 0:
+            raise RuntimeError(f"{n} values: need a positive multiple of 8 up to {self.cap}")
+        _native.check(_native.lib().dqg_peer_allreduce(
+            t.data_ptr(), t.data_ptr(), n, self.peer_data, self.peer_flags, self.ctl.data_ptr(),
+            self.cap, self.rank, self.world, self.wait_ns,
+            torch.cuda.current_stream(self.device).cuda_stream))
+        return t
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (idempotent)."""
+        if self._opened is None:
+            return
+        for base in self._opened:
+            self._ipc.close(base)
+        self._opened = None

@@ -107,6 +107,16 @@ int dqg_device_status(int device, uint32_t *status, int reset);
 int dqg_set_weight_prefetch(int enable);
 
 /*
+ * Process-wide choice of dqg_gemv's kernel, for tests and comparisons; returns
+ * the previous setting (or -1 for an invalid path). 0 (default): per shape,
+ * the direct kernel (group-wise formats whose group is one tensor-core step of
+ * a lane, activations within one CTA), else the streaming kernel, else the
+ * general one. 1: never the direct kernel. Results agree within the GEMV
+ * tolerance; each kernel is deterministic. No reference counterpart.
+ */
+int dqg_set_gemv_path(int path);
+
+/*
  * Diagnostic for the bounded-wait path: launches the streaming GEMV kernel for
  * this shape with its copy-issuing warp doing nothing, so that every wait in
  * the kernel gives up after wait_ns (1 ms to 1 s) and the kernel returns with
@@ -118,6 +128,41 @@ int dqg_debug_gemv_starved(const int32_t *qweight, const void *scales, const voi
                            void *y, const void *x, int64_t M, int64_t N, int64_t K,
                            int64_t bits, int64_t group_size, int symmetric, int interleaved,
                            uint64_t wait_ns, void *stream);
+
+/*
+ * Tensor-parallel plumbing: CUDA IPC of device memory between the processes
+ * of one node (no reference counterpart; the reference has no multi-GPU
+ * code, dequant/byte_model.py:179-251 only models the decoder's bytes).
+ * dqg_ipc_export writes the 64-byte IPC handle of the allocation holding ptr
+ * and ptr's byte offset in it; dqg_ipc_open maps a peer's handle into this
+ * process (base address of the peer allocation); dqg_ipc_close unmaps it.
+ */
+int dqg_ipc_export(const void *ptr, void *handle, uint64_t *offset);
+int dqg_ipc_open(const void *handle, void **base);
+int dqg_ipc_close(void *base);
+
+/*
+ * One-shot all-reduce (sum) of n fp16 values (n a multiple of 8, at most cap)
+ * across `world` ranks of one node, out = sum over ranks of in (in == out is
+ * allowed), summed in rank order in fp32 and rounded once, so every rank gets
+ * the same bits. Replaces the NCCL all-reduce that follows each row-parallel
+ * layer of the decoder step (the reference has none; it models the bytes in
+ * dequant/byte_model.py:179-251).
+ *   peer_data[r]  : rank r's exchange buffer, 2 * cap fp16, 16-byte aligned
+ *                   (this rank's own buffer at r == rank, IPC mappings of the
+ *                   others), zero-initialised once;
+ *   peer_flags[r] : rank r's flag array, ceil(cap / 2048) * world uint32,
+ *                   zero-initialised once;
+ *   ctl           : this rank's two uint32 call counters, zero-initialised once.
+ * Every rank must make the same sequence of calls. Each wait for a peer is
+ * bounded by wait_ns (0 = 2 s); a wait that runs out sets bit 0 of
+ * dqg_device_status and leaves out unwritten. Peer memory is read with plain
+ * loads only (no bulk copies, no multicast). Host arrays peer_data and
+ * peer_flags are read during the call only; nothing is allocated.
+ */
+int dqg_peer_allreduce(const void *in, void *out, int64_t n, const uint64_t *peer_data,
+                       const uint64_t *peer_flags, uint32_t *ctl, int64_t cap, int rank,
+                       int world, uint64_t wait_ns, void *stream);
 
 /*
  * The streaming GEMV kernel's launch plan for a shape (host arithmetic only,
@@ -157,6 +202,26 @@ int dqg_rope_kv_append(const void *qkv, const float *cos_row, const float *sin_r
                        void *k_cache, void *v_cache, int64_t M, int64_t n_q_heads,
                        int64_t n_kv_heads, int64_t head_dim, int64_t pos, int64_t capacity,
                        void *stream);
+
+/*
+ * Decode attention: one query token per sequence over its KV cache.
+ * q is [M, Hq, 128] (rotated), k_cache/v_cache are [M, Hkv, capacity, 128]
+ * with positions 0..T-1 valid, Hq a multiple of Hkv (at most 16 query heads
+ * per KV head, grouped consecutively); out[m, h] = softmax(q[m, h] .
+ * K[m, h / (Hq / Hkv), :T]^T / sqrt(128)) V[...], fp32 softmax, fp16 out.
+ * workspace: dqg_decode_attention_workspace(M, Hq, Hkv, T) bytes or more,
+ * 16-byte aligned, zeroed once before its first use and then left to the
+ * library (it keeps its split counters at zero between calls); calls that
+ * share a workspace must not overlap on the GPU. The split of positions over
+ * CTAs depends on T and the device's SM count, and the workspace needed grows
+ * with T: size it for the largest T (the cache capacity).
+ */
+int dqg_decode_attention_workspace(int64_t M, int64_t n_q_heads, int64_t n_kv_heads, int64_t T,
+                                   uint64_t *bytes);
+int dqg_decode_attention(const void *q, const void *k_cache, const void *v_cache, void *out,
+                         void *workspace, uint64_t workspace_bytes, int64_t M, int64_t n_q_heads,
+                         int64_t n_kv_heads, int64_t head_dim, int64_t T, int64_t capacity,
+                         void *stream);
 
 /*
  * SwiGLU: gate_up is [M, 2 I] (gate columns, then up columns);

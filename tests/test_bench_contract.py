@@ -1,5 +1,5 @@
 """The reference arm of bench.py (CPU only) prints one JSON line with the
-contract's keys, on the GPU arm's metric, unit and config."""
+contract's keys, on the GPU arm's metric (decode tokens/s), unit and config."""
 
 from __future__ import annotations
 
@@ -23,8 +23,17 @@ def test_reference_arm_prints_one_contract_line():
     import bench
     assert b["impl"] == "reference" and b["metric"] == bench.METRIC and b["unit"] == bench.UNIT
     assert b["config"] == bench.workload_config(1)
-    assert b["steps"] == 1 and b["warmup"] == 3 and b["higher_is_better"] is True
+    assert b["steps"] >= 1 and b["warmup"] == 3 and b["higher_is_better"] is True
+    assert b["scaling"] == "strong"
     assert b["value"] > 0 and b["cpu_baseline"]["value"] == b["value"]
     assert b["cpu_baseline"]["kind"] == "port" and b["cpu_baseline"]["cores"] >= 1
     assert b["e2e"] == {"value": b["value"], "unit": b["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_launch_count_follows_the_step():
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from dequant_project_b200.decoder import LLAMA2_7B
+    assert bench.decode_launches(LLAMA2_7B, 1) == 32 * 9 + 2
+    assert bench.decode_launches(LLAMA2_7B, 8) == 32 * 11 + 2

@@ -11,7 +11,6 @@ layer, the vocabulary all-gather), and the argument checks.
 
 from __future__ import annotations
 
-import math
 import socket
 import time
 
@@ -19,6 +18,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from decoder_reference import max_rel_err, reference_step
 from dequant_project_b200.decoder import DecoderConfig, TPDecoder, cat_rows
 from dequant_project_b200.packer import QuantConfig, dequantize, quantize_tensor
 
@@ -38,57 +38,15 @@ def free_port():
         return s.getsockname()[1]
 
 
-def reference_step(dec: TPDecoder, tokens, pos):
-    """fp32 Llama decode step from the decoder's own (world 1) weights and
-    caches, written out per head; returns logits [M, vocab] fp32."""
-    cfg, d = dec.cfg, dec.cfg.head_dim
-    m = tokens.shape[0]
-    h = dec.embed[tokens].float()
-    inv = cfg.rope_theta ** (-torch.arange(0, d, 2, dtype=torch.float64) / d)
-    ang = pos * inv
-    cos = torch.cat([ang.cos(), ang.cos()]).float()
-    sin = torch.cat([ang.sin(), ang.sin()]).float()
-
-    def norm(x):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.eps)
-
-    def rope(t):
-        half = d // 2
-        return t * cos + torch.cat([-t[..., half:], t[..., :half]], dim=-1) * sin
-
-    nq, nkv = cfg.n_heads * d, cfg.n_kv_heads * d
-    group = cfg.n_heads // cfg.n_kv_heads
-    for layer, w in enumerate(dec.layers):
-        qkv = norm(h) @ dequantize(w["qkv"]).float().t()
-        q = rope(qkv[:, :nq].reshape(m, cfg.n_heads, d))
-        k = rope(qkv[:, nq:nq + nkv].reshape(m, cfg.n_kv_heads, d))
-        v = qkv[:, nq + nkv:].reshape(m, cfg.n_kv_heads, d)
-        kc = dec.k_cache[layer][:, :, :pos].float()
-        vc = dec.v_cache[layer][:, :, :pos].float()
-        out = torch.empty(m, cfg.n_heads, d)
-        for b in range(m):
-            for hh in range(cfg.n_heads):
-                kv = hh // group
-                keys = torch.cat([kc[b, kv], k[b, kv][None]])
-                vals = torch.cat([vc[b, kv], v[b, kv][None]])
-                p = torch.softmax(keys @ q[b, hh] / math.sqrt(d), dim=0)
-                out[b, hh] = p @ vals
-        h = h + out.reshape(m, nq) @ dequantize(w["o"]).float().t()
-        gu = norm(h) @ dequantize(w["gu"]).float().t()
-        i = cfg.intermediate
-        act = torch.nn.functional.silu(gu[:, :i]) * gu[:, i:]
-        h = h + act @ dequantize(w["down"]).float().t()
-    return norm(h) @ dequantize(dec.lm_head).float().t()
-
-
 def test_single_rank_matches_fp32_reference():
     dec = TPDecoder(TINY, QCFG, seed=3, batch=2, kv_len=24, linear_fn=cpu_linear)
     tokens = torch.tensor([5, 977])
     pos = dec.kv_len
     ref = reference_step(dec, tokens, pos)        # reads the cache before the step writes it
+    ref16 = reference_step(dec, tokens, pos, storage=torch.float16)
     logits = dec.step(tokens, pos).float()
-    err = (logits - ref).abs().max() / ref.abs().max()
-    assert err < 1e-2, err
+    assert max_rel_err(logits, ref) < 1e-2
+    assert max_rel_err(logits, ref16) < 2e-3
 
 
 def test_step_writes_cache_slot_and_is_repeatable():
@@ -120,20 +78,21 @@ def test_rejects_head_counts_that_do_not_split():
         TPDecoder(TINY, QCFG, world=3, linear_fn=cpu_linear)
 
 
-@pytest.mark.parametrize("fmt", [(4, 64, False), (8, None, True), (2, 64, False)],
-                         ids=("int4-g64", "int8-perchannel", "int2-g64"))
-def test_gloo_two_ranks_match_one_rank(fmt):
-    world = 2
+def run_gloo_decoder(world, fmt, cfg_kw=None, batch=2, kv_len=24, tokens=(5, 977),
+                     limit_s=300):
+    """Spawn ``world`` gloo ranks of tp_workers.decoder_step; returns their
+    logits by rank (asserting every rank succeeded)."""
+    import tp_workers
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    import tp_workers
-    procs = [ctx.Process(target=tp_workers.decoder_step, args=(r, world, port, q, fmt))
+    procs = [ctx.Process(target=tp_workers.decoder_step,
+                         args=(r, world, port, q, fmt, cfg_kw, batch, kv_len, tokens))
              for r in range(world)]
     for p in procs:
         p.start()
     out, t0 = {}, time.time()
-    while len(out) < world and time.time() - t0 < 240:
+    while len(out) < world and time.time() - t0 < limit_s:
         try:
             r, status, val = q.get(timeout=1)
             out[r] = (status, val)
@@ -144,14 +103,55 @@ def test_gloo_two_ranks_match_one_rank(fmt):
         p.join(timeout=30)
         if p.is_alive():
             p.kill()
-    assert set(out) == {0, 1}, out
+    assert set(out) == set(range(world)), out
     for r, (status, val) in out.items():
         assert status == "ok", val
-    assert torch.equal(out[0][1], out[1][1])
+    return {r: val for r, (_, val) in out.items()}
+
+
+@pytest.mark.parametrize("fmt", [(4, 64, False), (8, None, True), (2, 64, False)],
+                         ids=("int4-g64", "int8-perchannel", "int2-g64"))
+def test_gloo_two_ranks_match_one_rank(fmt):
+    out = run_gloo_decoder(2, fmt)
+    assert torch.equal(out[0], out[1])
     one = TPDecoder(TINY, QuantConfig(*fmt), seed=3, batch=2, kv_len=24, linear_fn=cpu_linear)
     ref = one.step(torch.tensor([5, 977]), one.kv_len).float()
-    err = (out[0][1].float() - ref).abs().max() / ref.abs().max()
-    assert err < 5e-3, err
+    assert max_rel_err(out[0], ref) < 5e-3
+
+
+# Llama-2-7B-shaped (multi-head attention, 11008 = 86 groups of 128 split 11/10
+# over 8 ranks -> here 43 groups of 64 split 6/5) and Llama-3-70B-shaped
+# (grouped KV heads, one KV head per rank at width 8) small decoders; uneven
+# vocabulary split.
+WIDE_MHA = dict(n_layers=2, hidden=512, n_heads=16, n_kv_heads=16, intermediate=43 * 64,
+                vocab=1003)
+WIDE_GQA = dict(n_layers=2, hidden=512, n_heads=16, n_kv_heads=8, intermediate=43 * 64,
+                vocab=1003, rope_theta=500000.0)
+
+
+@pytest.mark.parametrize("world", (4, 8))
+@pytest.mark.parametrize("cfg_kw", (WIDE_MHA, WIDE_GQA), ids=("mha-7b-like", "gqa-70b-like"))
+def test_gloo_wide_tensor_parallel_matches_one_rank(world, cfg_kw):
+    """Every tensor-parallel width the scaling bench runs: heads split several
+    per rank (or one KV head per rank), the intermediate split unevenly on
+    group boundaries, the vocabulary unevenly; all ranks return the same
+    logits, which match the one-rank decoder and the fp32 restatement."""
+    fmt = (4, 64, False)
+    cfg = DecoderConfig(**cfg_kw)
+    from dequant_project_b200.tensor_parallel import intermediate_bounds
+    b = intermediate_bounds(cfg.intermediate, QuantConfig(*fmt), world)
+    sizes = {b[i + 1] - b[i] for i in range(world)}
+    assert len(sizes) == 2, sizes                          # uneven by one group
+    out = run_gloo_decoder(world, fmt, cfg_kw, batch=2, kv_len=20, tokens=(11, 1001))
+    for r in range(1, world):
+        assert torch.equal(out[r], out[0])
+    one = TPDecoder(cfg, QuantConfig(*fmt), seed=3, batch=2, kv_len=20, linear_fn=cpu_linear)
+    tokens = torch.tensor([11, 1001])
+    ref32 = reference_step(one, tokens, 20, storage=torch.float16)
+    ref = one.step(tokens, 20).float()
+    assert max_rel_err(out[0], ref) < 5e-3
+    assert max_rel_err(out[0], ref32) < 5e-3
+    assert max_rel_err(ref, ref32) < 5e-3
 
 
 def test_step_bytes_follow_the_reference_decode_model():

@@ -323,6 +323,39 @@ def test_graph_capture_replays_live_input():
     assert torch.equal(y, eager2)
 
 
+@pytest.fixture
+def streaming_only():
+    """dqg_gemv restricted to the streaming (and general) kernels."""
+    lib = _native.lib()
+    prev = lib.dqg_set_gemv_path(1)
+    yield
+    lib.dqg_set_gemv_path(prev)
+
+
+@pytest.mark.parametrize("m", (1, 3, 8))
+@pytest.mark.parametrize("n,k", [(4096, 11008), (11008, 4096), (3072, 3072), (149, 640)])
+@pytest.mark.parametrize("fmt", [(4, 128, False), (2, 64, False), (4, 128, True), (8, 64, False)],
+                         ids=("int4-g128-asym", "int2-g64-asym", "int4-g128-sym", "int8-g64-asym"))
+def test_streaming_kernel_on_direct_shapes(streaming_only, fmt, n, k, m):
+    """Shapes the direct kernel takes by default, through the streaming
+    kernel: it stays correct for every caller that forces it."""
+    run_case(n, k, *fmt, "sequential", m, seed=n + m)
+
+
+@pytest.mark.parametrize("m", (1, 2, 4, 8))
+@pytest.mark.parametrize("fmt", [(4, 128, False), (2, 64, False), (4, 64, True), (2, 128, False),
+                                 (8, 64, False), (4, 32, False)],
+                         ids=lambda f: f"int{f[0]}-g{f[1]}-{'sym' if f[2] else 'asym'}")
+def test_direct_kernel_formats(fmt, m):
+    """Every group size whose group is one tensor-core step of a lane (the
+    direct kernel's domain), interleaved and sequential, ragged rows and a
+    group count that is not a whole number of units."""
+    bits, gs, sym = fmt
+    for n, k in ((1000, 43 * gs), (37, 11 * gs), (4096, 4096)):
+        run_case(n, k, bits, gs, sym, "sequential", m, seed=n + m)
+        run_case(n, k, bits, gs, sym, "interleaved", m, seed=n + m + 1)
+
+
 def test_no_kernel_gave_up_a_wait():
     torch.cuda.synchronize()
     assert _native.device_status(torch.cuda.current_device()) == 0

@@ -82,17 +82,21 @@ def tp_rank_fails(rank, world, port, queue):
         queue.put((rank, "error", f"{type(exc).__name__}: {exc}", None))
 
 
-def decoder_step(rank, world, port, queue, fmt=(4, 64, False)):
-    """One decode step of the tiny test decoder on this gloo rank."""
+TINY_CFG = dict(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640, vocab=1000)
+
+
+def decoder_step(rank, world, port, queue, fmt=(4, 64, False), cfg_kw=None, batch=2,
+                 kv_len=24, tokens=(5, 977)):
+    """One decode step of a small test decoder (TINY_CFG unless ``cfg_kw``)
+    on this gloo rank; reports the all-gathered logits."""
     try:
         from dequant_project_b200.decoder import DecoderConfig, TPDecoder
         from dequant_project_b200.packer import QuantConfig
-        dist = _init(rank, world, port, "gloo", 60)
-        cfg = DecoderConfig(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, intermediate=640,
-                            vocab=1000)
-        dec = TPDecoder(cfg, QuantConfig(*fmt), world=world, rank=rank, seed=3, batch=2,
-                        kv_len=24, linear_fn=_cpu_linear)
-        out = dec.step(torch.tensor([5, 977]), dec.kv_len)
+        dist = _init(rank, world, port, "gloo", 120)
+        cfg = DecoderConfig(**(cfg_kw or TINY_CFG))
+        dec = TPDecoder(cfg, QuantConfig(*fmt), world=world, rank=rank, seed=3, batch=batch,
+                        kv_len=kv_len, linear_fn=_cpu_linear)
+        out = dec.step(torch.tensor(list(tokens)), dec.kv_len)
         queue.put((rank, "ok", out))
         dist.barrier()
         dist.destroy_process_group()
@@ -146,3 +150,140 @@ def decoder_rank_fails(rank, world, port, queue):
         queue.put((rank, "completed", None))
     except Exception as exc:
         queue.put((rank, "error", f"{type(exc).__name__}: {exc}"))
+
+
+def peer_allreduce_check(rank, world, port, queue):
+    """The peer all-reduce on this NCCL rank: several sizes eagerly, then the
+    same calls replayed twice from a CUDA graph; each result must equal the
+    fp32 sum of every rank's input in rank order, rounded once (bit-exact)."""
+    try:
+        from dequant_project_b200.peer_reduce import PeerAllReduce
+        dist = _init(rank, world, port, "nccl", 60)
+        dev = torch.device("cuda", rank)
+        ar = PeerAllReduce(None, dev, 65536)
+
+        def inputs(seed, n):
+            g = torch.Generator(device=dev).manual_seed(seed)
+            return [torch.randn(n, generator=g, device=dev).half() for _ in range(world)]
+
+        def expect(xs):
+            acc = torch.zeros_like(xs[0], dtype=torch.float32)
+            for x in xs:
+                acc += x.float()
+            return acc.half()
+
+        sizes = [8, 4096, 8192, 2 * 2048 + 24, 65536]
+        for i, n in enumerate(sizes):
+            xs = inputs(100 + i, n)
+            t = xs[rank].clone()
+            ar(t)
+            torch.cuda.synchronize(dev)
+            if not torch.equal(t, expect(xs)):
+                raise AssertionError(f"eager n={n}: not the rank-ordered fp32 sum")
+        bufs = [inputs(200 + i, n)[rank].clone() for i, n in enumerate(sizes)]
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        work = [b.clone() for b in bufs]
+        with torch.cuda.graph(g, stream=side):
+            for w in work:
+                ar(w)
+        for rep in range(2):
+            for w, b in zip(work, bufs):
+                w.copy_(b)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            for i, (w, n) in enumerate(zip(work, sizes)):
+                if not torch.equal(w, expect(inputs(200 + i, n))):
+                    raise AssertionError(f"graph replay {rep} n={n}: wrong sum")
+        g.reset()
+        from dequant_project_b200 import _native
+        if _native.device_status(rank) != 0:
+            raise AssertionError("a wait gave up")
+        ar.close()
+        queue.put((rank, "ok", None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        queue.put((rank, "error", traceback.format_exc()))
+
+
+def decoder_peer_vs_nccl(rank, world, port, queue):
+    """The small GPU test decoder on this NCCL rank with the peer all-reduce
+    and with NCCL's; both within 5e-3 of each other (the peer sum rounds once,
+    NCCL's fp16 sum per step). Reports the peer decoder's logits."""
+    try:
+        from dequant_project_b200.decoder import DecodeGraph, DecoderConfig, TPDecoder
+        from dequant_project_b200.packer import QuantConfig
+        dist = _init(rank, world, port, "nccl", 60)
+        cfg = DecoderConfig(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=4,
+                            intermediate=2816, vocab=5000)
+        dev = torch.device("cuda", rank)
+        tokens = torch.tensor([3, 4001], device=dev)
+        outs = {}
+        for mode in ("peer", "nccl"):
+            dec = TPDecoder(cfg, QuantConfig(4, 128, False), world=world, rank=rank, device=dev,
+                            seed=5, batch=2, kv_len=100, allreduce=mode)
+            eager = dec.step(tokens, 100).clone()
+            gr = DecodeGraph(dec, 100)
+            gr.tokens.copy_(tokens)
+            rep = gr.replay().clone()
+            torch.cuda.synchronize(dev)
+            gr.release()
+            dec.close()
+            if not torch.equal(rep, eager):
+                raise AssertionError(f"{mode}: graph replay differs from the eager step")
+            outs[mode] = eager
+        a, b = outs["peer"].float(), outs["nccl"].float()
+        err = ((a - b).abs().max() / b.abs().max()).item()
+        if err > 5e-3:
+            raise AssertionError(f"peer vs nccl decoder logits differ by {err}")
+        queue.put((rank, "ok", outs["peer"].cpu()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        queue.put((rank, "error", traceback.format_exc()))
+
+
+class FakeIpc:
+    """Stand-in for CUDA IPC on CPU ranks: a handle names (rank, pointer);
+    opening returns a fake base and records what was opened and closed."""
+
+    def __init__(self, rank):
+        self.rank, self.opened, self.closed = rank, [], []
+
+    def export(self, ptr):
+        return f"rank{self.rank}:{ptr}".encode().ljust(64, b"\0"), 16
+
+    def open(self, handle):
+        self.opened.append(handle.rstrip(b"\0").decode())
+        return 1 << 40 | len(self.opened) << 20
+
+    def close(self, base):
+        self.closed.append(base)
+
+
+def peer_exchange(rank, world, port, queue):
+    """PeerAllReduce's set-up on gloo CPU ranks with FakeIpc: reports which
+    handles this rank opened and the pointer tables it built."""
+    try:
+        from dequant_project_b200.peer_reduce import PeerAllReduce
+        dist = _init(rank, world, port, "gloo", 60)
+        ipc = FakeIpc(rank)
+        ar = PeerAllReduce(None, torch.device("cpu"), 5000, ipc=ipc)
+        info = {"opened": list(ipc.opened), "data": list(ar.peer_data),
+                "flags": list(ar.peer_flags), "own": ar.buffer.data_ptr(), "cap": ar.cap,
+                "chunks": ar.chunks, "nbytes": ar.buffer.numel()}
+        ar.close()
+        ar.close()
+        info["closed"] = len(ipc.closed)
+        try:
+            ar(torch.zeros(8, dtype=torch.float16))
+            info["after_close"] = "accepted"
+        except RuntimeError as exc:
+            info["after_close"] = str(exc)
+        queue.put((rank, "ok", info))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        queue.put((rank, "error", traceback.format_exc()))
