@@ -24,7 +24,9 @@ Sub-keys: ``decode_batch8`` (same model, batch 8); ``decode_70b`` (N >= 2,
 Llama-3-70B architecture, INT4 g128 and INT2 g64, batch 1
 and 8, 4096-token cache); ``gemv_sweep`` (N = 1: the 18
 bit-width sweep GEMVs as one graph, with per-case µs, and ``shape_sweep``,
-BASELINE config 3).
+BASELINE config 3; both also time the reference's own CUDA kernel, built
+unmodified for sm_100a by baseline/build_reference_kernel.py, on the same
+cases).
 
 ``--impl reference`` times the reference's CPU path for the same token (its
 GEMVs ``F.linear(x, packer.dequantize(W))`` as the C restatement in oracle/,
@@ -206,7 +208,11 @@ def gemv_sweep(args, dev, peaks):
     if not args.no_detail:
         out["detail"] = per_case_detail(dev, cs, data, peaks)
         try:
-            out["shape_sweep"] = shape_sweep(dev, peaks)
+            out["reference_kernel"] = reference_kernel_detail(dev, cs, data, peaks, out["detail"])
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
+            out["reference_kernel"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        try:
+            out["shape_sweep"] = shape_sweep(dev, peaks, with_reference=True)
         except Exception as exc:  # noqa: BLE001 - reported, never fatal to the line
             out["shape_sweep"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if not args.no_cpu:
@@ -339,7 +345,38 @@ SHAPE_SWEEP = [(4096, 4096), (12288, 4096), (4096, 14336), (28672, 8192), (8192,
                (128256, 4096)]
 
 
-def shape_sweep(dev, peaks):
+REF_KERNEL = ROOT / "baseline" / "_ref" / "ext" / "dequant_cuda_ref.so"
+
+
+def reference_kernel():
+    """The reference's own CUDA extension built for sm_100a by
+    baseline/build_reference_kernel.py, or None when it is not built."""
+    if not REF_KERNEL.exists():
+        return None
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("dequant_cuda_ref", REF_KERNEL)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def reference_kernel_detail(dev, cs, data, peaks, ours):
+    """µs per case of the reference kernel (kernels/dequant_gemv.cu:144-217,
+    unmodified, compiled for sm_100a) measured exactly like ``detail``, with
+    this library's µs beside it."""
+    mod = reference_kernel()
+    if mod is None:
+        return {"error": "reference kernel not built (python baseline/build_reference_kernel.py "
+                         "REFERENCE_ROOT)"}
+    rows = per_case_detail(dev, cs, data, peaks, reps=10, gemv_fn=mod.gemv)
+    ours_us = {r["case"]: r["us"] for r in ours}
+    for r in rows:
+        r["ours_us"] = ours_us.get(r["case"])
+        r["speedup"] = round(r["us"] / r["ours_us"], 3) if r.get("ours_us") else None
+    return rows
+
+
+def shape_sweep(dev, peaks, with_reference=False):
     """INT4 g128 asymmetric at batch 1 over the six shapes,
     per-case µs and GB/s measured like ``per_case_detail`` (distinct weight
     copies replayed from one graph, more bytes than L2 per replay)."""
@@ -357,15 +394,19 @@ def shape_sweep(dev, peaks):
         cs.append((n, k, 4, 128, False, 1, "int4-g128-asym"))
         data.append((pw, x))
     rows = per_case_detail(dev, cs, data, peaks, min_copies=4)
+    if with_reference:
+        ref = reference_kernel_detail(dev, cs, data, peaks, rows)
+        rows = {"ours": rows, "reference_kernel": ref}
     del data
     torch.cuda.empty_cache()
     return rows
 
 
-def per_case_detail(dev, cs, data, peaks, reps=20, min_copies=28):
+def per_case_detail(dev, cs, data, peaks, reps=20, min_copies=28, gemv_fn=None):
     import torch
 
     from dequant_project_b200 import dequant_cuda
+    gemv = gemv_fn or dequant_cuda.gemv
 
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
     rows = []
@@ -377,7 +418,7 @@ def per_case_detail(dev, cs, data, peaks, reps=20, min_copies=28):
 
         def run():
             for q, s, z in ws:
-                dequant_cuda.gemv(x, q, s, z, bits, gs or k, sym, False)
+                gemv(x, q, s, z, bits, gs or k, sym, False)
 
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
@@ -515,11 +556,11 @@ def cpu_baseline(cs, data, budget_s=10.0):
     gbs, el, passes = time_cpu_sweep(sample, threads, budget_s)
     # The same sample on one thread, as a second row (a short budget).
     gbs1, el1, passes1 = time_cpu_sweep(sample, 1, min(5.0, budget_s))
-    return {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port",
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"the 18 sweep cases on the first N/8 rows of each weight; {passes} passes "
                       f"in {el:.1f} s; C restatement of F.linear(x, packer.dequantize(pw)), "
                       f"OpenMP, {threads} threads",
-            "single_thread": {"value": round(gbs1, 3), "unit": UNIT, "cores": 1,
+            "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
                               "sample": f"same sample, {passes1} passes in {el1:.1f} s"}}
 
 

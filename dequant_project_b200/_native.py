@@ -62,6 +62,9 @@ def lib() -> ctypes.CDLL:
     h.dqg_peer_allreduce.restype = i32
     h.dqg_peer_allreduce.argtypes = [vp, vp, i64, u64p, u64p, vp, i64, i32, i32,
                                      ctypes.c_uint64, vp]
+    h.dqg_gemv_allreduce.restype = i32
+    h.dqg_gemv_allreduce.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32,
+                                     u64p, u64p, vp, i64, i32, i32, ctypes.c_uint64, vp]
     h.dqg_decode_attention_workspace.restype = i32
     h.dqg_decode_attention_workspace.argtypes = [i64, i64, i64, i64, u64p]
     h.dqg_decode_attention.restype = i32
@@ -78,6 +81,7 @@ EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_deq
             "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul",
             "dqg_stream_plan", "dqg_set_weight_prefetch", "dqg_debug_gemv_starved",
             "dqg_set_gemv_path", "dqg_decode_attention_workspace", "dqg_decode_attention",
+            "dqg_gemv_allreduce",
             "dqg_ipc_export", "dqg_ipc_open", "dqg_ipc_close", "dqg_peer_allreduce")
 
 

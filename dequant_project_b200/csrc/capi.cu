@@ -101,15 +101,17 @@ struct DirectEntry {
 };
 
 bool cached_direct_plan(int M, int N, int K, int bits, int group_size, int sms,
-                        dqg::DirectPlan* out) {
-  thread_local DirectEntry cache[32] = {};
+                        dqg::DirectPlan* out, bool fused = false) {
+  thread_local DirectEntry cache_plain[32] = {};
+  thread_local DirectEntry cache_fused[32] = {};
+  DirectEntry* cache = fused ? cache_fused : cache_plain;
   const uint32_t h = (static_cast<uint32_t>(M) * 2654435761u) ^ (static_cast<uint32_t>(N) * 40503u) ^
                      (static_cast<uint32_t>(K) * 2246822519u) ^ static_cast<uint32_t>(bits << 3) ^
                      static_cast<uint32_t>(group_size) * 3266489917u ^ static_cast<uint32_t>(sms);
   DirectEntry& e = cache[(h ^ (h >> 15)) & 31];
   if (!(e.used && e.M == M && e.N == N && e.K == K && e.bits == bits &&
         e.group_size == group_size && e.sms == sms)) {
-    e.ok = dqg::plan_direct(M, N, K, bits, group_size, sms, &e.plan);
+    e.ok = dqg::plan_direct(M, N, K, bits, group_size, sms, &e.plan, fused);
     e.M = M; e.N = N; e.K = K; e.bits = bits; e.group_size = group_size; e.sms = sms;
     e.used = true;
   }
@@ -118,7 +120,8 @@ bool cached_direct_plan(int M, int N, int K, int bits, int group_size, int sms,
 }
 
 // 0: pick the kernel per shape (direct, else streaming, else general);
-// 1: never the direct kernel (tests and comparisons).
+// 1: never the direct kernel; 2: the direct kernel wherever it has a plan
+// (tests and comparisons).
 std::atomic<int> g_gemv_path{0};
 
 int sm_count(int dev) {
@@ -253,11 +256,12 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   // whose activations fit one CTA; else the streaming kernel whenever its
   // plan fits (activations resident per CTA or per split-K cluster,
   // 16-byte-aligned scales/zeros); the general kernel otherwise.
-  if (g_gemv_path.load() == 0) {
+  const int path = g_gemv_path.load();
+  if (path != 1) {
     dqg::DirectPlan dplan;
     if (cached_direct_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
                            static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
-                           &dplan)) {
+                           &dplan, path == 2)) {
       e = dqg::launch_direct(a, dplan, static_cast<cudaStream_t>(stream));
       if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
       return ok();
@@ -416,6 +420,67 @@ int dqg_stream_plan(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group
   return ok();
 }
 
+int dqg_gemv_allreduce(const void* x, const int32_t* qweight, const void* scales,
+                       const void* zeros, void* y, int64_t M, int64_t N, int64_t K, int64_t bits,
+                       int64_t group_size, int symmetric, int interleaved,
+                       const uint64_t* peer_data, const uint64_t* peer_flags, uint32_t* ctl,
+                       int64_t cap, int rank, int world, uint64_t wait_ns, void* stream) {
+  if (world < 2 || world > dqg::kArMaxRanks || rank < 0 || rank >= world)
+    return fail(DQG_ERR_INVALID, "rank %d / world %d out of range (2 to %d ranks)", rank, world,
+                dqg::kArMaxRanks);
+  if (M < 1 || M > dqg::kMaxM)
+    return fail(DQG_ERR_INVALID, "gemv handles 1 <= M <= %d, got M=%lld", dqg::kMaxM,
+                (long long)M);
+  int rc = check_weight_args(qweight, scales, zeros, N, K, bits, group_size, symmetric);
+  if (rc) return rc;
+  if (x == nullptr || y == nullptr || peer_data == nullptr || peer_flags == nullptr ||
+      ctl == nullptr)
+    return fail(DQG_ERR_INVALID, "pointers must not be null");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(qweight) % 16)
+    return fail(DQG_ERR_INVALID, "x and qweight must be 16-byte aligned");
+  if (M * N > cap)
+    return fail(DQG_ERR_INVALID, "M * N = %lld exceeds the exchange capacity %lld",
+                (long long)(M * N), (long long)cap);
+  if (wait_ns != 0 && (wait_ns < 1000000ull || wait_ns > 10000000000ull))
+    return fail(DQG_ERR_INVALID, "wait_ns must be 0 (default) or in [1 ms, 10 s]");
+  for (int r = 0; r < world; ++r)
+    if (peer_data[r] == 0 || peer_flags[r] == 0 || peer_data[r] % 16 || peer_flags[r] % 4)
+      return fail(DQG_ERR_INVALID, "peer buffers of rank %d missing or misaligned", r);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  dqg::DirectPlan dplan;
+  if (!cached_direct_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                          static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
+                          &dplan, true) ||
+      dplan.grid > dqg::kArMaxCtas)
+    return fail(DQG_ERR_UNSUPPORTED, "no fused row-parallel plan for this shape");
+  dqg::GemvArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.qweight = reinterpret_cast<const uint32_t*>(qweight);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.zeros = static_cast<const uint16_t*>(zeros);
+  a.y = static_cast<uint16_t*>(y);
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.bits = static_cast<int>(bits);
+  a.group_size = static_cast<int>(group_size);
+  a.symmetric = symmetric != 0;
+  a.interleaved = interleaved != 0;
+  dqg::PeerGemvArgs ar;
+  ar.rank = rank;
+  ar.world = world;
+  ar.data = reinterpret_cast<const unsigned long long*>(peer_data);
+  ar.flags = reinterpret_cast<const unsigned long long*>(peer_flags);
+  ar.ctl = ctl;
+  ar.cap = cap;
+  ar.wait_ns = wait_ns ? wait_ns : 2000000000ull;
+  e = dqg::launch_direct(a, dplan, static_cast<cudaStream_t>(stream), &ar);
+  if (e != cudaSuccess) return cuda_fail(e, "row-parallel gemv launch");
+  return ok();
+}
+
 int dqg_decode_attention_workspace(int64_t M, int64_t n_q_heads, int64_t n_kv_heads,
                                    int64_t T, uint64_t* bytes) {
   if (bytes == nullptr) return fail(DQG_ERR_INVALID, "bytes must not be null");
@@ -476,9 +541,10 @@ int dqg_decode_attention(const void* q, const void* k_cache, const void* v_cache
   p.S = dqg::attention_splits(p.M, p.Hkv, p.T, sm_count(dev), &p.Ts);
   const size_t mh = static_cast<size_t>(M) * n_kv_heads;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  p.part = reinterpret_cast<float*>(ws);
-  p.ml = reinterpret_cast<float*>(ws + mh * p.S * p.g * 128 * 4);
-  p.tickets = reinterpret_cast<unsigned*>(ws + mh * p.S * p.g * 128 * 4 + mh * p.S * p.g * 2 * 4);
+  const size_t cnt = dqg::attention_counter_bytes(p.M, p.Hkv);
+  p.tickets = reinterpret_cast<unsigned*>(ws);
+  p.ml = reinterpret_cast<float*>(ws + cnt);
+  p.part = reinterpret_cast<float*>(ws + cnt + mh * p.S * p.g * 2 * 4);
   p.scale_log2 = static_cast<float>(1.4426950408889634 / 11.313708498984761);  // log2(e)/sqrt(128)
   e = dqg::launch_decode_attention(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode attention launch");
@@ -486,7 +552,7 @@ int dqg_decode_attention(const void* q, const void* k_cache, const void* v_cache
 }
 
 int dqg_set_gemv_path(int path) {
-  if (path != 0 && path != 1) return -1;
+  if (path < 0 || path > 2) return -1;
   return g_gemv_path.exchange(path);
 }
 

@@ -211,6 +211,36 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// ---- peer memory (other GPUs' buffers mapped through CUDA IPC) ----
+
+// Store / acquire-load of a flag at system scope (visible across GPUs).
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// Wait until *flag >= epoch (wrap-safe), bounded by limit_ns; false (and the
+// timeout bit in g_status) when the limit ran out.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* flag, uint32_t epoch,
+                                              uint64_t limit_ns) {
+  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  while (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) < 0) {
+    if (globaltimer() - t0 > limit_ns) {
+      atomicOr(&g_status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Named barrier among a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -284,6 +284,10 @@ __global__ void __launch_bounds__(kAttnThreads)
 
 }  // namespace
 
+size_t attention_counter_bytes(int M, int Hkv) {
+  return (static_cast<size_t>(M) * Hkv * 4 + 255) / 256 * 256;
+}
+
 int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out) {
   const int mh = M * Hkv;
   int s = (2 * num_sms + mh - 1) / mh;
@@ -296,9 +300,15 @@ int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out) {
 }
 
 size_t attention_workspace_bytes(int M, int Hq, int Hkv, int T, int num_sms) {
-  const int S = attention_splits(M, Hkv, T, num_sms, nullptr);
-  const size_t mh = static_cast<size_t>(M) * Hkv, g = Hq / Hkv;
-  return mh * S * g * kD * 4 + mh * S * g * 2 * 4 + mh * 4;
+  // Split counters first (a fixed place for every T), then the partials,
+  // sized for the most splits any T up to this one can take.
+  const int mh = M * Hkv;
+  int s_max = (2 * num_sms + mh - 1) / mh;
+  const int t_tiles = (T + kTileT - 1) / kTileT;
+  if (s_max > t_tiles) s_max = t_tiles;
+  if (s_max < 1) s_max = 1;
+  const size_t g = Hq / Hkv;
+  return attention_counter_bytes(M, Hkv) + static_cast<size_t>(mh) * s_max * g * (kD + 2) * 4;
 }
 
 cudaError_t launch_decode_attention(const AttnParams& p, cudaStream_t stream) {

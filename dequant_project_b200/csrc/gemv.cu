@@ -636,7 +636,8 @@ cudaError_t read_device_status(int device, uint32_t* status, bool reset) {
   if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
   cudaError_t (*readers[])(uint32_t*, bool) = {read_status_gemv, read_status_stream_b2,
                                                 read_status_stream_b4, read_status_stream_b8,
-                                                read_status_peer};
+                                                read_status_peer,        read_status_direct_b2,
+                                                read_status_direct_b4,   read_status_direct_b8};
   *status = 0;
   for (auto rd : readers) {
     uint32_t v = 0;

@@ -129,6 +129,25 @@ struct StreamPlan {
 
 bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, StreamPlan* plan);
 
+// ------------------------------------------------------- peer all-reduce
+// One-shot all-reduce of fp16 tensors over peer memory (peer_reduce.cu).
+constexpr int kArChunk = 2048;    // elements per CTA (one flag per chunk and rank)
+constexpr int kArMaxRanks = 8;
+
+struct PeerReduceParams {
+  const __half* in;
+  __half* out;
+  long long n;                    // elements, a multiple of 8
+  long long cap;                  // elements per parity half of each exchange buffer
+  unsigned long long peer_data[kArMaxRanks];   // each rank's exchange buffer (2 * cap fp16)
+  unsigned long long peer_flags[kArMaxRanks];  // each rank's flags [chunks][world] u32
+  uint32_t* ctl;                  // this rank's [epoch, ticket]
+  int rank, world;
+  unsigned long long wait_ns;
+};
+
+cudaError_t launch_peer_allreduce(const PeerReduceParams& p, cudaStream_t stream);
+
 // ------------------------------------------------------------------ direct
 // Direct kernel (gemv_direct.cuh): group-wise formats with one MMA step per
 // group, activations resident in one CTA; every warp streams its own range of
@@ -155,14 +174,37 @@ struct DirectParams {
   int xp;                 // bytes per permuted activation row in shared memory
   int off_x, off_sx, off_zero, off_red, off_tiles, off_ring;
   int prefetch;           // 1: first ring issued before the dependent-launch wait
+  // Row-parallel mode (ar_world > 1): y = the sum over ranks of every rank's
+  // x_r @ W_r^T, exchanged through peer memory (see PeerGemvArgs).
+  int ar_rank, ar_world;
+  unsigned long long ar_data[kArMaxRanks];   // each rank's fp32 exchange buffer [2][M * N]
+  unsigned long long ar_flags[kArMaxRanks];  // each rank's flags [CTA][world] u32
+  uint32_t* ar_ctl;                          // this rank's [epoch, ticket]
+  long long ar_cap;                          // fp32 values per parity half
+  unsigned long long ar_wait_ns;
 };
+
+// Peer memory of a row-parallel GEMV (dqg_gemv_allreduce).
+struct PeerGemvArgs {
+  int rank, world;
+  const unsigned long long* data;    // [world] exchange buffers (fp32, 2 * cap values)
+  const unsigned long long* flags;   // [world] flag arrays (kArMaxCtas * world u32)
+  uint32_t* ctl;
+  long long cap;
+  unsigned long long wait_ns;
+};
+constexpr int kArMaxCtas = 1024;
 
 struct DirectPlan {
   int wpl, mp, gs, Gp, xp, off_x, off_sx, off_zero, off_red, off_tiles, off_ring, smem, grid;
 };
 
-bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, DirectPlan* plan);
-cudaError_t launch_direct(const GemvArgs& args, const DirectPlan& plan, cudaStream_t stream);
+// fused: plan for the row-parallel GEMV + all-reduce (any M); otherwise only
+// where the direct kernel measured faster than the streaming one.
+bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, DirectPlan* plan,
+                 bool fused = false);
+cudaError_t launch_direct(const GemvArgs& args, const DirectPlan& plan, cudaStream_t stream,
+                          const PeerGemvArgs* ar = nullptr);
 
 // ------------------------------------------------------- decode attention
 struct AttnParams {
@@ -177,6 +219,7 @@ struct AttnParams {
   float scale_log2;       // log2(e) / sqrt(128)
 };
 int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out);
+size_t attention_counter_bytes(int M, int Hkv);
 size_t attention_workspace_bytes(int M, int Hq, int Hkv, int T, int num_sms);
 cudaError_t launch_decode_attention(const AttnParams& p, cudaStream_t stream);
 
@@ -209,25 +252,11 @@ cudaError_t read_status_stream_b2(uint32_t* status, bool reset);
 cudaError_t read_status_stream_b4(uint32_t* status, bool reset);
 cudaError_t read_status_stream_b8(uint32_t* status, bool reset);
 cudaError_t read_status_peer(uint32_t* status, bool reset);
+cudaError_t read_status_direct_b2(uint32_t* status, bool reset);
+cudaError_t read_status_direct_b4(uint32_t* status, bool reset);
+cudaError_t read_status_direct_b8(uint32_t* status, bool reset);
 
-// ------------------------------------------------------- peer all-reduce
-// One-shot all-reduce of fp16 tensors over peer memory (peer_reduce.cu).
-constexpr int kArChunk = 2048;    // elements per CTA (one flag per chunk and rank)
-constexpr int kArMaxRanks = 8;
 
-struct PeerReduceParams {
-  const __half* in;
-  __half* out;
-  long long n;                    // elements, a multiple of 8
-  long long cap;                  // elements per parity half of each exchange buffer
-  unsigned long long peer_data[kArMaxRanks];   // each rank's exchange buffer (2 * cap fp16)
-  unsigned long long peer_flags[kArMaxRanks];  // each rank's flags [chunks][world] u32
-  uint32_t* ctl;                  // this rank's [epoch, ticket]
-  int rank, world;
-  unsigned long long wait_ns;
-};
-
-cudaError_t launch_peer_allreduce(const PeerReduceParams& p, cudaStream_t stream);
 
 cudaError_t launch_add_one(const float* x, float* out, int64_t n, cudaStream_t stream);
 

@@ -18,7 +18,8 @@ namespace {
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 }  // namespace
 
-bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, DirectPlan* plan) {
+bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, DirectPlan* plan,
+                 bool fused) {
   if (M < 1 || M > kMaxM || N < 1 || num_sms < 1 || group_size <= 0 || K % group_size) return false;
   const int wpl = gemv_words_per_lane(bits, group_size, K);
   if (wpl == 0) return false;
@@ -27,12 +28,14 @@ bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, Dir
   // Group-wise formats whose group is exactly one MMA step of the lane
   // layout (INT4 up to g128, INT2 up to g256, INT8 up to g64).
   if (G < 2 || group_size != sc) return false;
-  // Measured on B200 against the streaming kernel: the direct kernel is
-  // faster for 4- and 8-bit codes on rows of up to 6144 codes (INT4 g128:
-  // 4096x4096 6.85 -> 5.66 us, 128256x4096 108 -> 80 us, M = 8 11008x4096
-  // 17.8 -> 15.6 us) and slower on longer rows (28672x8192 36.9 -> 39.7 us)
-  // and for 2-bit codes (4-byte copies per lane); those stay streaming.
+  // Measured on B200 against the streaming kernel, inside the Llama-2-7B
+  // decode step (INT4 g128): at batch 8 the direct kernel takes the step from
+  // 4.52 to 4.09 ms/token, at batch 1 it costs 2.28 -> 2.55 ms; on rows longer
+  // than 6144 codes and for 2-bit codes (4-byte copies per lane) it is slower
+  // in isolation too. The fused row-parallel GEMV has no streaming form and
+  // takes any batch.
   if (bits < 4 || K > 6144) return false;
+  if (!fused && M < 5) return false;
   int mp = 1;
   while (mp < M) mp <<= 1;
   const int gs = 8 / mp;
@@ -67,7 +70,8 @@ bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, Dir
   return true;
 }
 
-cudaError_t launch_direct(const GemvArgs& a, const DirectPlan& pl, cudaStream_t stream) {
+cudaError_t launch_direct(const GemvArgs& a, const DirectPlan& pl, cudaStream_t stream,
+                          const PeerGemvArgs* ar) {
   DirectParams p;
   p.x = a.x;
   p.qw = a.qweight;
@@ -87,6 +91,26 @@ cudaError_t launch_direct(const GemvArgs& a, const DirectPlan& pl, cudaStream_t 
   p.off_tiles = pl.off_tiles;
   p.off_ring = pl.off_ring;
   p.prefetch = weight_prefetch() ? 1 : 0;
+  p.ar_rank = 0;
+  p.ar_world = 1;
+  p.ar_ctl = nullptr;
+  p.ar_wait_ns = 0;
+  p.ar_cap = 0;
+  for (int r = 0; r < kArMaxRanks; ++r) p.ar_data[r] = p.ar_flags[r] = 0;
+  if (ar != nullptr && ar->world > 1) {
+    if (ar->world > kArMaxRanks || pl.grid > kArMaxCtas ||
+        static_cast<long long>(a.M) * a.N > ar->cap)
+      return cudaErrorInvalidValue;
+    p.ar_rank = ar->rank;
+    p.ar_world = ar->world;
+    p.ar_ctl = ar->ctl;
+    p.ar_wait_ns = ar->wait_ns;
+    p.ar_cap = ar->cap;
+    for (int r = 0; r < ar->world; ++r) {
+      p.ar_data[r] = ar->data[r];
+      p.ar_flags[r] = ar->flags[r];
+    }
+  }
   switch (a.bits) {
     case 2: return launch_direct_b2(pl.wpl, pl.gs, a.symmetric, a.interleaved, p, pl.grid, pl.smem, stream);
     case 4: return launch_direct_b4(pl.wpl, pl.gs, a.symmetric, a.interleaved, p, pl.grid, pl.smem, stream);

@@ -304,6 +304,21 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
   }
   __syncthreads();
 
+  // Row-parallel mode: this rank's fp32 partial of y goes to its exchange
+  // buffer (parity of this call's epoch) instead of y.
+  const bool ar = p.ar_world > 1;
+  const uint32_t ep = ar ? *reinterpret_cast<volatile const uint32_t*>(p.ar_ctl) + 1u : 0u;
+  // Parity halves are a fixed cap apart, so that calls of different shapes
+  // never write into the half a slower peer may still read.
+  const int64_t ar_par = static_cast<int64_t>(ep & 1u) * p.ar_cap;
+  auto store_out = [&](int xrow, int row, float v) {
+    const int64_t e = static_cast<int64_t>(xrow) * p.N + row;
+    if (ar)
+      reinterpret_cast<float*>(p.ar_data[p.ar_rank])[ar_par + e] = v;
+    else
+      p.y[e] = __half_as_ushort(__float2half_rn(v));
+  };
+
   // ---------------------------------------------------------------- main loop
   const int my_slot = gid / MP;
   const int my_xrow = gid - my_slot * MP;
@@ -402,9 +417,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
         const int xrow = (2 * c + (e & 1)) & (MP - 1);
         if (xrow < p.M) {
           if (whole) {
-            if (r0 + row < row_end)
-              p.y[static_cast<int64_t>(xrow) * p.N + r0 + row] =
-                  __half_as_ushort(__float2half_rn(a[e]));
+            if (r0 + row < row_end) store_out(xrow, r0 + row, a[e]);
           } else {
             rs[row * 8 + xrow] = a[e];
           }
@@ -465,8 +478,49 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
         if (tiles[w * 2] == t) sum += rw[row * 8 + xrow];
         if (tiles[w * 2 + 1] == t) sum += rw[kTile * 8 + row * 8 + xrow];
       }
-      if (r0 + row < row_end)
-        p.y[static_cast<int64_t>(xrow) * p.N + r0 + row] = __half_as_ushort(__float2half_rn(sum));
+      if (r0 + row < row_end) store_out(xrow, r0 + row, sum);
+    }
+  }
+  if (!ar) return;
+
+  // Row-parallel exchange: once this CTA's rows are in its exchange buffer,
+  // raise its flag on every rank, wait (bounded) for every rank's flag of
+  // this CTA, and sum the ranks' partials of these rows in rank order.
+  __syncthreads();
+  if (threadIdx.x < p.ar_world) {
+    fence_acq_rel_sys();
+    st_relaxed_sys(reinterpret_cast<uint32_t*>(p.ar_flags[threadIdx.x]) +
+                       blockIdx.x * p.ar_world + p.ar_rank,
+                   ep);
+  }
+  bool ok = true;
+  if (threadIdx.x < p.ar_world) {
+    ok = wait_flag_sys(reinterpret_cast<const uint32_t*>(p.ar_flags[p.ar_rank]) +
+                           blockIdx.x * p.ar_world + threadIdx.x,
+                       ep, p.ar_wait_ns);
+    fence_acq_rel_sys();
+  }
+  ok = __syncthreads_and(ok);
+  const int rows = row_end - row_begin;
+  if (ok) {
+    for (int idx = threadIdx.x; idx < rows * p.M; idx += kDirectThreads) {
+      const int xrow = idx / rows, row = row_begin + idx - (idx / rows) * rows;
+      const int64_t e = ar_par + static_cast<int64_t>(xrow) * p.N + row;
+      float sum = 0.f;
+      for (int r = 0; r < p.ar_world; ++r)
+        sum += __ldcg(reinterpret_cast<const float*>(p.ar_data[r]) + e);
+      p.y[static_cast<int64_t>(xrow) * p.N + row] = __half_as_ushort(__float2half_rn(sum));
+    }
+  }
+  // The last CTA of the call advances the epoch.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(p.ar_ctl + 1, 1u);
+    if (t == gridDim.x - 1) {
+      p.ar_ctl[1] = 0u;
+      __threadfence();
+      atomicExch(p.ar_ctl, ep);
     }
   }
 }

@@ -9,3 +9,5 @@ cudaError_t launch_direct_b4(int wpl, int gs, bool sym, bool inter, const Direct
 }
 
 }  // namespace dqg
+
+DQG_STATUS_READER(read_status_direct_b4)

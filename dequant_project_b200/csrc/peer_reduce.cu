@@ -38,17 +38,7 @@ namespace {
 
 constexpr int kArThreads = 256;
 
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fence_sys() { fence_acq_rel_sys(); }
 
 // 16 bytes from a (possibly peer) address, bypassing L1: the data were written
 // by another GPU during this call.
@@ -88,16 +78,7 @@ __global__ void __launch_bounds__(kArThreads)
   if (tid < p.world) {
     const uint32_t* f = reinterpret_cast<const uint32_t*>(p.peer_flags[p.rank]) +
                         chunk * p.world + tid;
-    if (static_cast<int32_t>(ld_acquire_sys(f) - ep) < 0) {
-      const uint64_t t0 = globaltimer();
-      while (static_cast<int32_t>(ld_acquire_sys(f) - ep) < 0) {
-        if (globaltimer() - t0 > p.wait_ns) {
-          atomicOr(&g_status, kStatusWaitTimeout);
-          ok = false;
-          break;
-        }
-      }
-    }
+    ok = wait_flag_sys(f, ep, p.wait_ns);
     fence_sys();
   }
   ok = __syncthreads_and(ok);

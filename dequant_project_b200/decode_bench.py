@@ -245,6 +245,8 @@ def save_model(args, device) -> None:
 
 
 def run(args) -> dict | None:
+    from dequant_project_b200 import _native
+    _native.lib().dqg_set_gemv_path(args.gemv_path)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -288,6 +290,8 @@ def _parser() -> argparse.ArgumentParser:
                     help="pack the model once, write it to this file and exit")
     ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
                     help="collective after the row-parallel layers (world > 1)")
+    ap.add_argument("--gemv-path", type=int, default=0, choices=(0, 1),
+                    help="dqg_set_gemv_path: 0 = per shape (default), 1 = no direct kernel")
     ap.add_argument("--check-tp1", action="store_true",
                     help="rank 0 compares the logits with the model on one GPU")
     return ap

@@ -332,6 +332,14 @@ class TPDecoder:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
 
+    def _row_parallel(self, x: torch.Tensor, pw: PackedWeight) -> torch.Tensor:
+        """A row-parallel layer: the fused GEMV + peer all-reduce on CUDA ranks
+        with the peer collective (one kernel where the shape has a fused
+        plan), else this rank's GEMV and the all-reduce."""
+        if self._peer is not None and self._linear is _default_linear:
+            return self._peer.gemv(x, pw)
+        return self._all_reduce(self._linear(x, pw))
+
     def _lm_head(self, x: torch.Tensor) -> torch.Tensor:
         if isinstance(self.lm_head, PackedWeight):
             return self._linear(x, self.lm_head)
@@ -362,10 +370,10 @@ class TPDecoder:
             kc, vc = self.k_cache[layer], self.v_cache[layer]
             q = ops.rope_kv_append(qkv, cos, sin, kc, vc, pos, self.hq, self.hkv)
             a = ops.attention(q, kc, vc, pos + 1, self._attn_ws)
-            o = self._all_reduce(self._linear(a.reshape(m, nq), w["o"]))
+            o = self._row_parallel(a.reshape(m, nq), w["o"])
             x = ops.add_rms_norm(h, o, self.mlp_norm[layer], cfg.eps)
             act = ops.silu_mul(self._linear(x, w["gu"]))
-            pending = self._all_reduce(self._linear(act, w["down"]))
+            pending = self._row_parallel(act, w["down"])
         x = ops.add_rms_norm(h, pending, self.final_norm, cfg.eps)
         logits = self._lm_head(x)
         if self.world == 1:

@@ -14,7 +14,11 @@ algorithms with one exchange round through memory every rank can address:
 * each call (``dqg_peer_allreduce`` in libdequant_b200.so) copies the input
   into this rank's buffer, raises a flag in every peer's flag array, waits
   (bounded) for every peer's flag and sums all ranks' buffers in rank order in
-  fp32 with one rounding, so every rank gets the same bits.
+  fp32 with one rounding, so every rank gets the same bits;
+* ``gemv`` runs a row-parallel layer as ONE kernel (``dqg_gemv_allreduce``):
+  the GEMV's CTAs write their rows' fp32 partials into this buffer and
+  exchange them through the same peer mappings while other CTAs still stream
+  weights; shapes without a fused plan take the GEMV, then the all-reduce.
 
 The call counter lives on the device, so calls can be captured in a CUDA graph
 and replayed. All ranks must make the same sequence of calls, as with any
@@ -32,6 +36,7 @@ from dequant_project_b200 import _native
 
 CHUNK = 2048          # elements per CTA of the kernel (one flag per chunk and rank)
 MAX_RANKS = 8
+MAX_GEMV_CTAS = 1024  # flags of the fused row-parallel GEMV: one per CTA and rank
 HANDLE_BYTES = 64     # sizeof(cudaIpcMemHandle_t)
 
 
@@ -79,12 +84,18 @@ class PeerAllReduce:
         self.chunks = (self.cap + CHUNK - 1) // CHUNK
         self.wait_ns = int(wait_ns)
         self._ipc = ipc if ipc is not None else CudaIpc()
-        data_bytes = 2 * self.cap * 2
-        flag_bytes = self.chunks * self.world * 4
-        # One allocation: [exchange data | flags], so one handle per rank.
-        self.buffer = torch.zeros(data_bytes + flag_bytes, dtype=torch.uint8, device=self.device)
-        self.ctl = torch.zeros(2, dtype=torch.int32, device=self.device)
+        # One allocation, so one handle per rank: [exchange data (fp32, two
+        # parity halves of cap values; the fp16 all-reduce uses its front) |
+        # all-reduce flags | fused-GEMV flags].
+        data_bytes = 2 * self.cap * 4
+        ar_flag_bytes = self.chunks * self.world * 4
+        gemv_flag_bytes = MAX_GEMV_CTAS * self.world * 4
+        self.buffer = torch.zeros(data_bytes + ar_flag_bytes + gemv_flag_bytes,
+                                  dtype=torch.uint8, device=self.device)
+        # Call counters: [all-reduce epoch, ticket, fused-GEMV epoch, ticket].
+        self.ctl = torch.zeros(4, dtype=torch.int32, device=self.device)
         self._flag_off = data_bytes
+        self._gemv_flag_off = data_bytes + ar_flag_bytes
         handle, offset = self._ipc.export(self.buffer.data_ptr())
         infos = [None] * self.world
         dist.all_gather_object(infos, (self.rank, handle, offset), group=group)
@@ -101,6 +112,8 @@ class PeerAllReduce:
                 data_ptrs.append(base + off)
         self.peer_data = (ctypes.c_uint64 * self.world)(*data_ptrs)
         self.peer_flags = (ctypes.c_uint64 * self.world)(*[p + self._flag_off for p in data_ptrs])
+        self.peer_gemv_flags = (ctypes.c_uint64 * self.world)(
+            *[p + self._gemv_flag_off for p in data_ptrs])
         # No rank may raise a flag in a buffer its peer has not mapped yet.
         dist.barrier(group=group)
 
@@ -118,6 +131,31 @@ class PeerAllReduce:
             self.cap, self.rank, self.world, self.wait_ns,
             torch.cuda.current_stream(self.device).cuda_stream))
         return t
+
+    def gemv(self, x: torch.Tensor, pw) -> torch.Tensor:
+        """Row-parallel layer: the sum over ranks of ``x_r @ W_r^T`` for this
+        rank's slice ``x`` [M, K_r] and packed ``pw`` [N, K_r]; fp16 [M, N],
+        the same on every rank."""
+        from dequant_project_b200 import quant_linear as ql
+        if self._opened is None:
+            raise RuntimeError("peer all-reduce used after close()")
+        n, k = pw.shape
+        x2 = x.reshape(-1, k).contiguous()
+        m = x2.shape[0]
+        bits, gs, sym, inter = ql._format_args(pw.config, k)
+        if m <= ql.MAX_M and m * n <= self.cap:
+            y = torch.empty((m, n), dtype=torch.float16, device=self.device)
+            rc = _native.lib().dqg_gemv_allreduce(
+                x2.data_ptr(), pw.qweight.data_ptr(), pw.scales.data_ptr(),
+                None if pw.zeros is None else pw.zeros.data_ptr(), y.data_ptr(), m, n, k, bits,
+                gs, int(sym), int(inter), self.peer_data, self.peer_gemv_flags,
+                self.ctl.data_ptr() + 8, self.cap, self.rank, self.world, self.wait_ns,
+                torch.cuda.current_stream(self.device).cuda_stream)
+            if rc == 0:
+                return y.view(*x.shape[:-1], n)
+            if rc != 2:                       # anything but "no fused plan" is an error
+                _native.check(rc)
+        return self(ql.gemv(x2, pw)).view(*x.shape[:-1], n)
 
     def close(self) -> None:
         """Unmap the peers' buffers (idempotent)."""

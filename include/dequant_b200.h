@@ -109,9 +109,10 @@ int dqg_set_weight_prefetch(int enable);
 /*
  * Process-wide choice of dqg_gemv's kernel, for tests and comparisons; returns
  * the previous setting (or -1 for an invalid path). 0 (default): per shape,
- * the direct kernel (group-wise formats whose group is one tensor-core step of
- * a lane, activations within one CTA), else the streaming kernel, else the
- * general one. 1: never the direct kernel. Results agree within the GEMV
+ * the direct kernel (4/8-bit group-wise formats whose group is one
+ * tensor-core step of a lane, rows of at most 6144 codes, M >= 5), else the
+ * streaming kernel, else the general one. 1: never the direct kernel. 2: the
+ * direct kernel wherever it applies, any M. Results agree within the GEMV
  * tolerance; each kernel is deterministic. No reference counterpart.
  */
 int dqg_set_gemv_path(int path);
@@ -165,6 +166,32 @@ int dqg_peer_allreduce(const void *in, void *out, int64_t n, const uint64_t *pee
                        int world, uint64_t wait_ns, void *stream);
 
 /*
+ * Row-parallel GEMV fused with its all-reduce: every rank passes its slice of
+ * the input dimension (x [M, K_r], W_r [N, K_r] packed, as dqg_gemv) and gets
+ * y = sum over ranks of x_r @ W_r^T, fp16 [M, N], the same bits on every rank.
+ * One kernel: each CTA writes its rows' fp32 partial into this rank's
+ * exchange buffer, raises its flag on every rank, waits (bounded by wait_ns,
+ * 0 = 2 s) for the same CTA's flag of every rank and sums the ranks' partials
+ * in rank order, reading peers with plain loads (no bulk copies, no
+ * multicast); CTAs that finish early exchange while the others still stream.
+ *   peer_data[r]  : rank r's exchange buffer, 2 * cap fp32 values, 16-byte
+ *                   aligned (IPC mappings for the peers); M * N <= cap;
+ *   peer_flags[r] : rank r's flag array, 1024 * world uint32, zeroed once;
+ *   ctl           : this rank's two uint32 call counters, zeroed once (not
+ *                   shared with dqg_peer_allreduce).
+ * Every rank must make the same sequence of calls. Returns
+ * DQG_ERR_UNSUPPORTED for shapes without a fused plan (then call dqg_gemv and
+ * dqg_peer_allreduce). Replaces gemv + the NCCL all-reduce that follows each
+ * row-parallel layer; the reference has neither (it models the bytes in
+ * dequant/byte_model.py:179-251).
+ */
+int dqg_gemv_allreduce(const void *x, const int32_t *qweight, const void *scales,
+                       const void *zeros, void *y, int64_t M, int64_t N, int64_t K, int64_t bits,
+                       int64_t group_size, int symmetric, int interleaved,
+                       const uint64_t *peer_data, const uint64_t *peer_flags, uint32_t *ctl,
+                       int64_t cap, int rank, int world, uint64_t wait_ns, void *stream);
+
+/*
  * The streaming GEMV kernel's launch plan for a shape (host arithmetic only,
  * no device access): out[0..22] = wpl, mp, ks, n_slabs, stages, n_meta,
  * w_pitch, xp, stage_bytes, C (cluster size), KC (codes per cluster rank),
@@ -213,8 +240,8 @@ int dqg_rope_kv_append(const void *qkv, const float *cos_row, const float *sin_r
  * 16-byte aligned, zeroed once before its first use and then left to the
  * library (it keeps its split counters at zero between calls); calls that
  * share a workspace must not overlap on the GPU. The split of positions over
- * CTAs depends on T and the device's SM count, and the workspace needed grows
- * with T: size it for the largest T (the cache capacity).
+ * CTAs depends on T and the device's SM count; a workspace sized for some T
+ * serves every call with fewer positions (size it for the cache capacity).
  */
 int dqg_decode_attention_workspace(int64_t M, int64_t n_q_heads, int64_t n_kv_heads, int64_t T,
                                    uint64_t *bytes);

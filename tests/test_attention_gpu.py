@@ -84,3 +84,19 @@ def test_rejects_bad_arguments(cuda_device):
                                                         device=cuda_device))
     with pytest.raises(RuntimeError, match="workspace"):
         decode_ops.attention(q, kc, kc, 16, torch.zeros(16, dtype=torch.uint8, device=cuda_device))
+
+
+def test_one_workspace_serves_every_length(cuda_device):
+    """A workspace sized for the capacity, shared by calls of many lengths in
+    a row (different numbers of position splits), as the decoder's steps at
+    successive positions share it."""
+    m, hq, hkv, cap = 1, 32, 32, 2050
+    g = torch.Generator(device=cuda_device).manual_seed(9)
+    q = torch.randn(m, hq, D, generator=g, device=cuda_device).half()
+    kc = torch.randn(m, hkv, cap, D, generator=g, device=cuda_device).half()
+    vc = torch.randn(m, hkv, cap, D, generator=g, device=cuda_device).half()
+    ws = decode_ops.attention_workspace(m, hq, hkv, cap, cuda_device)
+    for T in (1900, 2049, 64, 1, 1000, 2050, 129):
+        out = decode_ops.attention(q, kc, vc, T, ws)
+        ref = fp32_attention(q, kc, vc, T)
+        assert ((out.float() - ref).abs().max() / ref.abs().max()).item() < 2e-3, T

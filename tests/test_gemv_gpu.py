@@ -342,14 +342,24 @@ def test_streaming_kernel_on_direct_shapes(streaming_only, fmt, n, k, m):
     run_case(n, k, *fmt, "sequential", m, seed=n + m)
 
 
+@pytest.fixture
+def direct_everywhere():
+    """dqg_gemv takes the direct kernel wherever it applies, at any M."""
+    lib = _native.lib()
+    prev = lib.dqg_set_gemv_path(2)
+    yield
+    lib.dqg_set_gemv_path(prev)
+
+
 @pytest.mark.parametrize("m", (1, 2, 4, 8))
-@pytest.mark.parametrize("fmt", [(4, 128, False), (2, 64, False), (4, 64, True), (2, 128, False),
-                                 (8, 64, False), (4, 32, False)],
+@pytest.mark.parametrize("fmt", [(4, 128, False), (4, 64, True), (8, 64, False), (4, 32, False),
+                                 (8, 32, True)],
                          ids=lambda f: f"int{f[0]}-g{f[1]}-{'sym' if f[2] else 'asym'}")
-def test_direct_kernel_formats(fmt, m):
-    """Every group size whose group is one tensor-core step of a lane (the
-    direct kernel's domain), interleaved and sequential, ragged rows and a
-    group count that is not a whole number of units."""
+def test_direct_kernel_formats(direct_everywhere, fmt, m):
+    """Every 4/8-bit group size whose group is one tensor-core step of a lane
+    (the direct kernel's domain), at every activation-row count, interleaved
+    and sequential, ragged rows and a group count that is not a whole number
+    of units."""
     bits, gs, sym = fmt
     for n, k in ((1000, 43 * gs), (37, 11 * gs), (4096, 4096)):
         run_case(n, k, bits, gs, sym, "sequential", m, seed=n + m)

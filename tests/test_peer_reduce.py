@@ -51,9 +51,11 @@ def test_gloo_ranks_exchange_and_map_every_peer(world):
             assert f"rank{s}:{out[s][1]['own']}" in info["opened"]
         assert info["data"][r] == info["own"]
         assert len(info["data"]) == world and len(set(info["data"])) == world
-        flag_off = 2 * info["cap"] * 2
+        flag_off = 2 * info["cap"] * 4                    # fp32 exchange data first
         assert [f - d for f, d in zip(info["flags"], info["data"])] == [flag_off] * world
+        gemv_off = flag_off + info["chunks"] * world * 4
+        assert [f - d for f, d in zip(info["gemv_flags"], info["data"])] == [gemv_off] * world
         assert info["cap"] == 5000 and info["chunks"] == 3
-        assert info["nbytes"] == flag_off + info["chunks"] * world * 4
+        assert info["nbytes"] == gemv_off + 1024 * world * 4
         assert info["closed"] == world - 1                # close() is idempotent
         assert "after close" in info["after_close"]

@@ -150,3 +150,70 @@ def test_two_gpu_decoder_peer_matches_nccl():
     import tp_workers
     out = _run_ranks(tp_workers.decoder_peer_vs_nccl, 2)
     assert torch.equal(out[0], out[1])
+
+
+def _packed_layer(n, k, seed, dev):
+    from dequant_project_b200.packer import QuantConfig, quantize_tensor
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = torch.randn(n, k, generator=g, device=dev).half() * 0.02
+    return quantize_tensor(w, QuantConfig(4, 128, False))
+
+
+@pytest.mark.parametrize("m", (1, 8))
+def test_fused_row_parallel_sums_a_ready_peer(cuda_device, m):
+    """dqg_gemv_allreduce on one GPU as rank 0 of 2, the other rank's partial
+    already in its exchange buffer with every CTA flag raised: y is this
+    rank's fp32 partial plus the peer's, rounded once; the partial itself is
+    what the plain GEMV rounds to fp16."""
+    from dequant_project_b200 import dequant_cuda
+    n, k, world, cap = 4096, 2048, 2, 8 * 4096
+    pw = _packed_layer(n, k, 3, cuda_device)
+    x = torch.randn(m, k, device=cuda_device).half()
+    flags_bytes = 1024 * world * 4
+    mine = torch.zeros(2 * cap * 4 + flags_bytes, dtype=torch.uint8, device=cuda_device)
+    peer = torch.zeros_like(mine)
+    ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    peer_part = torch.randn(m * n, device=cuda_device)
+    peer[:2 * cap * 4].view(torch.float32)[cap:cap + m * n] = peer_part   # epoch 1 -> half 1
+    mine[2 * cap * 4:].view(torch.int32)[1::2] = 7                        # rank 1 is ahead
+    y = torch.empty(m, n, dtype=torch.float16, device=cuda_device)
+    data = (ctypes.c_uint64 * 2)(mine.data_ptr(), peer.data_ptr())
+    flags = (ctypes.c_uint64 * 2)(mine.data_ptr() + 2 * cap * 4, peer.data_ptr() + 2 * cap * 4)
+    _native.device_status(cuda_device.index, reset=True)
+    _native.check(_native.lib().dqg_gemv_allreduce(
+        x.data_ptr(), pw.qweight.data_ptr(), pw.scales.data_ptr(), pw.zeros.data_ptr(),
+        y.data_ptr(), m, n, k, 4, 128, 0, 0, data, flags, ctl.data_ptr(), cap, 0, world, 0,
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    part = mine[:2 * cap * 4].view(torch.float32)[cap:cap + m * n]
+    assert torch.equal(y.view(-1), (part + peer_part).half())
+    plain = dequant_cuda.gemv(x, pw.qweight, pw.scales, pw.zeros, 4, 128, False, False)
+    assert torch.equal(part.half().view(m, n), plain)
+    assert ctl.tolist() == [1, 0]
+    assert _native.device_status(cuda_device.index) == 0
+
+
+def test_fused_row_parallel_missing_peer_reports(cuda_device):
+    n, k, world, cap = 1024, 1024, 2, 4096
+    pw = _packed_layer(n, k, 4, cuda_device)
+    x = torch.randn(1, k, device=cuda_device).half()
+    mine = torch.zeros(2 * cap * 4 + 1024 * world * 4, dtype=torch.uint8, device=cuda_device)
+    peer = torch.zeros_like(mine)
+    ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    y = torch.full((1, n), 5.0, dtype=torch.float16, device=cuda_device)
+    data = (ctypes.c_uint64 * 2)(mine.data_ptr(), peer.data_ptr())
+    flags = (ctypes.c_uint64 * 2)(mine.data_ptr() + 2 * cap * 4, peer.data_ptr() + 2 * cap * 4)
+    _native.device_status(cuda_device.index, reset=True)
+    _native.check(_native.lib().dqg_gemv_allreduce(
+        x.data_ptr(), pw.qweight.data_ptr(), pw.scales.data_ptr(), pw.zeros.data_ptr(),
+        y.data_ptr(), 1, n, k, 4, 128, 0, 0, data, flags, ctl.data_ptr(), cap, 0, world,
+        20_000_000, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert _native.device_status(cuda_device.index, reset=True) & 1
+    assert bool((y == 5.0).all())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_fused_row_parallel():
+    import tp_workers
+    _run_ranks(tp_workers.fused_row_parallel_check, 2)

@@ -272,7 +272,8 @@ def peer_exchange(rank, world, port, queue):
         ipc = FakeIpc(rank)
         ar = PeerAllReduce(None, torch.device("cpu"), 5000, ipc=ipc)
         info = {"opened": list(ipc.opened), "data": list(ar.peer_data),
-                "flags": list(ar.peer_flags), "own": ar.buffer.data_ptr(), "cap": ar.cap,
+                "flags": list(ar.peer_flags), "gemv_flags": list(ar.peer_gemv_flags),
+                "own": ar.buffer.data_ptr(), "cap": ar.cap,
                 "chunks": ar.chunks, "nbytes": ar.buffer.numel()}
         ar.close()
         ar.close()
@@ -283,6 +284,44 @@ def peer_exchange(rank, world, port, queue):
         except RuntimeError as exc:
             info["after_close"] = str(exc)
         queue.put((rank, "ok", info))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        queue.put((rank, "error", traceback.format_exc()))
+
+
+def fused_row_parallel_check(rank, world, port, queue):
+    """PeerAllReduce.gemv on this NCCL rank (INT4 g128 row-parallel layers,
+    M = 1 and 8, several calls and a graph replay): every rank gets the same
+    bits, within 2e-3 of the fp32 product over the full input dimension."""
+    try:
+        from dequant_project_b200.packer import QuantConfig, dequantize, quantize_tensor
+        from dequant_project_b200.peer_reduce import PeerAllReduce
+        from dequant_project_b200.tensor_parallel import shard_rows
+        dist = _init(rank, world, port, "nccl", 60)
+        dev = torch.device("cuda", rank)
+        ar = PeerAllReduce(None, dev, 8 * 4096)
+        for i, (n, k, m) in enumerate(((4096, 4096, 1), (4096, 11008, 8), (4096, 4096, 8))):
+            g = torch.Generator(device=dev).manual_seed(50 + i)
+            w = torch.randn(n, k, generator=g, device=dev).half() * 0.02
+            x = torch.randn(m, k, generator=g, device=dev).half()
+            pw = quantize_tensor(w, QuantConfig(4, 128, False))
+            shard, lo, hi = shard_rows(pw, world, rank)
+            y = ar.gemv(x[:, lo:hi].contiguous(), shard)
+            torch.cuda.synchronize(dev)
+            ref = x.float() @ dequantize(pw).float().t()
+            err = ((y.float() - ref).abs().max() / ref.abs().max()).item()
+            if err > 2e-3:
+                raise AssertionError(f"case {i}: rel err {err}")
+            ys = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(ys, y)
+            if any(not torch.equal(ys[0], t) for t in ys):
+                raise AssertionError(f"case {i}: ranks disagree")
+        from dequant_project_b200 import _native
+        if _native.device_status(rank) != 0:
+            raise AssertionError("a wait gave up")
+        ar.close()
+        queue.put((rank, "ok", None))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
