@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
     h.dqg_decode_attention.restype = i32
     h.dqg_decode_attention.argtypes = [vp, vp, vp, vp, vp, ctypes.c_uint64, i64, i64, i64, i64,
                                        i64, i64, vp]
+    h.dqg_decode_attention_noalloc.restype = i32
+    h.dqg_decode_attention_noalloc.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
     h.dqg_stream_plan.restype = i32
     h.dqg_stream_plan.argtypes = [i64, i64, i64, i64, i64, i32, ctypes.POINTER(ctypes.c_int32), i32]
     _lib = h
@@ -81,7 +83,7 @@ EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_deq
             "dqg_device_status", "dqg_add_rms_norm", "dqg_rope_kv_append", "dqg_silu_mul",
             "dqg_stream_plan", "dqg_set_weight_prefetch", "dqg_debug_gemv_starved",
             "dqg_set_gemv_path", "dqg_decode_attention_workspace", "dqg_decode_attention",
-            "dqg_gemv_allreduce",
+            "dqg_gemv_allreduce", "dqg_decode_attention_noalloc",
             "dqg_ipc_export", "dqg_ipc_open", "dqg_ipc_close", "dqg_peer_allreduce")
 
 

@@ -551,6 +551,53 @@ int dqg_decode_attention(const void* q, const void* k_cache, const void* v_cache
   return ok();
 }
 
+int dqg_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                 void* out, int64_t M, int64_t n_q_heads, int64_t n_kv_heads,
+                                 int64_t head_dim, int64_t T, int64_t capacity, void* stream) {
+  if (head_dim != 128)
+    return fail(DQG_ERR_UNSUPPORTED, "decode attention handles head_dim 128, got %lld",
+                (long long)head_dim);
+  uint64_t need = 0;
+  int rc = dqg_decode_attention_workspace(M, n_q_heads, n_kv_heads, T, &need);
+  if (rc) return rc;
+  if (need > dqg::attention_noalloc_capacity())
+    return fail(DQG_ERR_UNSUPPORTED,
+                "this call needs %llu bytes of scratch; the library's static scratch holds %llu "
+                "(use dqg_decode_attention with a workspace)",
+                (unsigned long long)need, (unsigned long long)dqg::attention_noalloc_capacity());
+  if (capacity < T)
+    return fail(DQG_ERR_INVALID, "T=%lld positions exceed the cache capacity %lld", (long long)T,
+                (long long)capacity);
+  if (M * n_kv_heads * capacity * head_dim > (int64_t(1) << 40))
+    return fail(DQG_ERR_INVALID, "cache too large");
+  const void* ptrs[4] = {q, k_cache, v_cache, out};
+  const char* names[4] = {"q", "k_cache", "v_cache", "out"};
+  for (int i = 0; i < 4; ++i) {
+    if (ptrs[i] == nullptr) return fail(DQG_ERR_INVALID, "%s must not be null", names[i]);
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16)
+      return fail(DQG_ERR_INVALID, "%s must be 16-byte aligned", names[i]);
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  dqg::AttnParams p;
+  p.q = static_cast<const __half*>(q);
+  p.kc = static_cast<const __half*>(k_cache);
+  p.vc = static_cast<const __half*>(v_cache);
+  p.o = static_cast<__half*>(out);
+  p.M = static_cast<int>(M);
+  p.Hq = static_cast<int>(n_q_heads);
+  p.Hkv = static_cast<int>(n_kv_heads);
+  p.g = p.Hq / p.Hkv;
+  p.cap = static_cast<int>(capacity);
+  p.T = static_cast<int>(T);
+  p.S = dqg::attention_splits(p.M, p.Hkv, p.T, sm_count(dev), &p.Ts);
+  p.scale_log2 = static_cast<float>(1.4426950408889634 / 11.313708498984761);  // log2(e)/sqrt(128)
+  e = dqg::launch_decode_attention_noalloc(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode attention (static scratch) launch");
+  return ok();
+}
+
 int dqg_set_gemv_path(int path) {
   if (path < 0 || path > 2) return -1;
   return g_gemv_path.exchange(path);

@@ -339,3 +339,57 @@ namespace {
 
 }  // namespace
 }  // namespace dqg
+
+// ---------------------------------------------------------------------------
+// Decode attention for callers that cannot allocate device memory.
+//
+// Some callers of this library cannot call cudaMalloc: a host that binds the
+// C ABI from a runtime whose device memory is all owned by another allocator
+// (an inference server that reserves the GPU's memory for KV caches at start-up
+// and hands each kernel only the step's tensors), or a plugin whose host gives
+// it no allocator and no workspace. dqg_decode_attention_noalloc serves them:
+// its scratch (split counters and per-split partials) is the file-scope array
+// below, so the caller passes only inputs and outputs.
+//
+// The array is a device symbol: every GPU that loads this library holds its
+// kNoAllocScratchBytes until the process exits. In host code its name is a
+// host-side stand-in, not a device address, so the launcher looks up the device
+// address once per device, with that device current, and passes it to the
+// kernel. Every call shares the array and it keeps the last call's contents:
+// the split counters are cleared on the stream before each launch, and calls
+// that overlap on the GPU (other streams, other host threads) race on it.
+namespace dqg {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB per GPU
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+}  // namespace
+
+size_t attention_noalloc_capacity() { return kNoAllocScratchBytes; }
+
+cudaError_t launch_decode_attention_noalloc(AttnParams p, cudaStream_t stream) {
+  static void* scratch[64] = {nullptr};  // device address of the array, per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (scratch[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_attn_scratch);
+    if (e != cudaSuccess) return e;
+    scratch[dev] = ptr;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(scratch[dev]);
+  const size_t mh = static_cast<size_t>(p.M) * p.Hkv;
+  const size_t cnt = attention_counter_bytes(p.M, p.Hkv);
+  if (cnt + mh * p.S * p.g * (kD + 2) * 4 > kNoAllocScratchBytes) return cudaErrorInvalidValue;
+  e = cudaMemsetAsync(ws, 0, cnt, stream);  // split counters start at zero
+  if (e != cudaSuccess) return e;
+  p.tickets = reinterpret_cast<unsigned*>(ws);
+  p.ml = reinterpret_cast<float*>(ws + cnt);
+  p.part = reinterpret_cast<float*>(ws + cnt + mh * p.S * p.g * 2 * 4);
+  return launch_decode_attention(p, stream);
+}
+
+}  // namespace dqg

@@ -222,6 +222,9 @@ int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out);
 size_t attention_counter_bytes(int M, int Hkv);
 size_t attention_workspace_bytes(int M, int Hq, int Hkv, int T, int num_sms);
 cudaError_t launch_decode_attention(const AttnParams& p, cudaStream_t stream);
+// The same kernel with its scratch in a static device array (no allocation).
+size_t attention_noalloc_capacity();
+cudaError_t launch_decode_attention_noalloc(AttnParams p, cudaStream_t stream);
 
 // Process-wide switch (default on): the streaming kernel issues its first
 // weight ring before waiting for the previous grid on the stream.

@@ -251,6 +251,25 @@ int dqg_decode_attention(const void *q, const void *k_cache, const void *v_cache
                          void *stream);
 
 /*
+ * Decode attention exactly as dqg_decode_attention, for callers that cannot
+ * allocate device memory (for example a host whose GPU memory is all owned by
+ * another allocator, such as a server that reserves it for KV caches at
+ * start-up and gives each kernel only the step's tensors): no workspace
+ * argument. No counterpart in the reference; it exists for such callers only.
+ * The scratch is a static array of 2 MiB inside the library, held by every GPU
+ * that loads the library until the process exits; a call whose split partials
+ * need more (dqg_decode_attention_workspace reports the size) is rejected with
+ * DQG_ERR_UNSUPPORTED. The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture. Every call shares the array: its split counters are cleared on the
+ * stream before each launch, and calls that overlap on the GPU race on it.
+ * Nothing is allocated (no cudaMalloc, no cudaFree).
+ */
+int dqg_decode_attention_noalloc(const void *q, const void *k_cache, const void *v_cache,
+                                 void *out, int64_t M, int64_t n_q_heads, int64_t n_kv_heads,
+                                 int64_t head_dim, int64_t T, int64_t capacity, void *stream);
+
+/*
  * SwiGLU: gate_up is [M, 2 I] (gate columns, then up columns);
  * out[m, i] = fp16(silu(gate) * up), silu(g) = g / (1 + exp(-g)) in fp32.
  */
