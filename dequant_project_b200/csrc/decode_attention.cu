@@ -41,6 +41,7 @@ constexpr int kStages = 3;
 constexpr int kRowBytes = kD * 2;  // one cache row (256 bytes)
 constexpr int kTileBytes = kTileT * kRowBytes;
 constexpr int kAttnSmem = kStages * 2 * kTileBytes;  // K and V tiles
+constexpr int kMaxSplits = 64;     // position splits per (sequence, KV head)
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
@@ -95,8 +96,11 @@ __global__ void __launch_bounds__(kAttnThreads)
   const __half* vbase = p.vc + mh * p.cap * kD;
   const uint32_t sbase = smem_u32(smem);
 
-  // The query and the newest cache slot come from the previous kernels.
+  // The query and the newest cache slot come from the previous kernels. The
+  // next kernel may be scheduled at once: it waits for this grid before it
+  // reads the output, and can stage its own inputs meanwhile.
   pdl_wait_prior_grid();
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   // Q as A fragments for the eight 16-wide steps over D: rows are the g query
   // heads of this KV head (rows >= g are zero).
@@ -204,7 +208,6 @@ __global__ void __launch_bounds__(kAttnThreads)
     __syncthreads();
   }
   cp_async_wait<0>();
-  pdl_launch_dependents();
 
   // Merge the four warps' (max, sum, O) in shared memory (the tiles are free).
 #pragma unroll
@@ -268,17 +271,60 @@ __global__ void __launch_bounds__(kAttnThreads)
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < g * kD; idx += kAttnThreads) {
-    const int j = idx / kD, d = idx - (idx / kD) * kD;
+  // Split weights first (max over splits, then exp2(m_s - max) / sum), staged
+  // in shared memory; then every output element is one weighted sum over the
+  // splits with independent loads.
+  float* wsplit = reinterpret_cast<float*>(smem);            // [S][g]: max, then weight
+  float* lsplit = wsplit + kMaxSplits * 16;                   // [S][g]: sum
+  float* wmax = lsplit + kMaxSplits * 16;                     // [g]
+  float* wden = wmax + 16;                                    // [g]
+  for (int i = threadIdx.x; i < S * g; i += kAttnThreads) {
+    wsplit[i] = __ldcg(pml + 2 * i);
+    lsplit[i] = __ldcg(pml + 2 * i + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < g) {
+    const int j = threadIdx.x;
     float mx = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, __ldcg(pml + (sp * g + j) * 2));
-    float num = 0.f, den = 0.f;
-    for (int sp = 0; sp < S; ++sp) {
-      const float f = exp2f(__ldcg(pml + (sp * g + j) * 2) - mx);
-      num += __ldcg(part + (sp * g + j) * kD + d) * f;
-      den += __ldcg(pml + (sp * g + j) * 2 + 1) * f;
+    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, wsplit[sp * g + j]);
+    float den = 0.f;
+    for (int sp = 0; sp < S; ++sp) den += lsplit[sp * g + j] * exp2f(wsplit[sp * g + j] - mx);
+    wmax[j] = mx;
+    wden[j] = den;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < S * g; i += kAttnThreads) {
+    const int j = i % g;
+    wsplit[i] = exp2f(wsplit[i] - wmax[j]) / wden[j];
+  }
+  __syncthreads();
+  // Each thread owns four consecutive outputs and sums over the splits in
+  // batches of 16 independent 16-byte loads (the partials were written by
+  // other CTAs moments ago and sit in L2; a loop with one load in flight
+  // at a time took 20 us for 33 splits of eight heads).
+  const int nv = g * (kD / 4);
+  const float4* part4 = reinterpret_cast<const float4*>(part);
+  for (int v = threadIdx.x; v < nv; v += kAttnThreads) {
+    const int j = v / (kD / 4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < S; sp += 16) {
+      float4 w[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        w[u] = sp + u < S ? __ldcg(part4 + static_cast<int64_t>(sp + u) * nv + v)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const float f = sp + u < S ? wsplit[(sp + u) * g + j] : 0.f;
+        acc.x += w[u].x * f;
+        acc.y += w[u].y * f;
+        acc.z += w[u].z * f;
+        acc.w += w[u].w * f;
+      }
     }
-    orow[j * kD + d] = __float2half_rn(num / den);
+    __half2* o2 = reinterpret_cast<__half2*>(orow + v * 4);
+    o2[0] = __floats2half2_rn(acc.x, acc.y);
+    o2[1] = __floats2half2_rn(acc.z, acc.w);
   }
 }
 
@@ -288,10 +334,15 @@ size_t attention_counter_bytes(int M, int Hkv) {
   return (static_cast<size_t>(M) * Hkv * 4 + 255) / 256 * 256;
 }
 
+#ifndef DQG_ATTN_CTAS_PER_SM
+#define DQG_ATTN_CTAS_PER_SM 2
+#endif
+
 int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out) {
   const int mh = M * Hkv;
-  int s = (2 * num_sms + mh - 1) / mh;
-  const int max_s = (T + kTileT - 1) / kTileT;
+  int s = (DQG_ATTN_CTAS_PER_SM * num_sms + mh - 1) / mh;
+  int max_s = (T + kTileT - 1) / kTileT;
+  if (max_s > kMaxSplits) max_s = kMaxSplits;
   if (s > max_s) s = max_s;
   if (s < 1) s = 1;
   const int ts = ((T + s - 1) / s + kTileT - 1) / kTileT * kTileT;
@@ -303,8 +354,9 @@ size_t attention_workspace_bytes(int M, int Hq, int Hkv, int T, int num_sms) {
   // Split counters first (a fixed place for every T), then the partials,
   // sized for the most splits any T up to this one can take.
   const int mh = M * Hkv;
-  int s_max = (2 * num_sms + mh - 1) / mh;
-  const int t_tiles = (T + kTileT - 1) / kTileT;
+  int s_max = (DQG_ATTN_CTAS_PER_SM * num_sms + mh - 1) / mh;
+  int t_tiles = (T + kTileT - 1) / kTileT;
+  if (t_tiles > kMaxSplits) t_tiles = kMaxSplits;
   if (s_max > t_tiles) s_max = t_tiles;
   if (s_max < 1) s_max = 1;
   const size_t g = Hq / Hkv;

@@ -162,6 +162,7 @@ constexpr int kDirectNW = DQG_DIRECT_NW;         // warps per CTA
 constexpr int kDirectThreads = 32 * kDirectNW;
 constexpr int kDirectRingBytes = DQG_DIRECT_RING;  // per-warp ring of packed words in flight
 constexpr int kDirectMaxSmem = 232448;
+constexpr int kDirectMinSmem = 120 * 1024;       // more than half an SM: one CTA per SM
 
 struct DirectParams {
   const uint16_t* x;

@@ -29,13 +29,12 @@ bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, Dir
   // layout (INT4 up to g128, INT2 up to g256, INT8 up to g64).
   if (G < 2 || group_size != sc) return false;
   // Measured on B200 against the streaming kernel, inside the Llama-2-7B
-  // decode step (INT4 g128): at batch 8 the direct kernel takes the step from
-  // 4.52 to 4.09 ms/token, at batch 1 it costs 2.28 -> 2.55 ms; on rows longer
-  // than 6144 codes and for 2-bit codes (4-byte copies per lane) it is slower
-  // in isolation too. The fused row-parallel GEMV has no streaming form and
-  // takes any batch.
+  // decode step (INT4 g128): with one CTA per SM (below) the direct kernel
+  // takes batch 1 from 2.305 to 2.229 ms/token and batch 8 from 4.54 to 4.16;
+  // on rows longer than 6144 codes and for 2-bit codes (4-byte copies per
+  // lane) it is slower than the streaming kernel.
   if (bits < 4 || K > 6144) return false;
-  if (!fused && M < 5) return false;
+  (void)fused;
   int mp = 1;
   while (mp < M) mp <<= 1;
   const int gs = 8 / mp;
@@ -64,6 +63,10 @@ bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, Dir
   off += kDirectNW * kDirectRingBytes;
   pl.smem = off;
   if (pl.smem > kDirectMaxSmem) return false;
+  // One CTA per SM: a smaller request lets the block scheduler put two CTAs
+  // of one launch on one SM (and none on another), which halves those CTAs'
+  // share of the SM and measured 2.23 -> 2.55 ms/token in the decode step.
+  if (pl.smem < kDirectMinSmem) pl.smem = kDirectMinSmem;
   const int tiles = (N + kTile - 1) / kTile;
   pl.grid = tiles < num_sms ? tiles : num_sms;
   *plan = pl;

@@ -580,17 +580,22 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks)
     named_sync(1, kStreamNCW * 32);
     // Prologue 2: the activation sum of every group (per-channel: of the
     // whole row); symmetric formats need none.
+    // A group of one step (spg == 1) has its sum already: the per-step sums
+    // are read as the group sums and this pass and its barrier are skipped.
+    const bool group_is_step = GROUPED && p.gsize == SC;
     if constexpr (SYM) {
     } else if constexpr (GROUPED) {
       const int spg = p.gsize / SC;
-      for (int e = tid; e < p.M * Gs; e += kCT) {
-        const int m = e / Gs;
-        const int g = e - m * Gs;
-        const float* src = sstep + m * spr + g * spg;
-        float sum = 0.f;
-        for (int t = 0; t < spg; ++t) sum += src[t];
-        sxg[e] = sum;
-      }
+      if (group_is_step) sxg = sstep;
+      else
+        for (int e = tid; e < p.M * Gs; e += kCT) {
+          const int m = e / Gs;
+          const int g = e - m * Gs;
+          const float* src = sstep + m * spr + g * spg;
+          float sum = 0.f;
+          for (int t = 0; t < spg; ++t) sum += src[t];
+          sxg[e] = sum;
+        }
     } else {
       if (cw < p.M) {
         float sum = 0.f;
@@ -600,7 +605,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks)
         if (lane == 0) sxg[cw] = sum;
       }
     }
-    named_sync(1, kStreamNCW * 32);
+    if (!SYM && !group_is_step) named_sync(1, kStreamNCW * 32);
     if (tid == 0) mbar_arrive(sx_ready);
 
     // Main loop. Work units (grouped: gslots consecutive groups; per-channel:

@@ -54,6 +54,7 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
 __global__ void __launch_bounds__(kArThreads)
     peer_allreduce_kernel(const __grid_constant__ PeerReduceParams p) {
   pdl_wait_prior_grid();
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const int chunk = blockIdx.x;
   const int tid = threadIdx.x;
   const uint32_t ep = *reinterpret_cast<volatile const uint32_t*>(p.ctl) + 1u;
@@ -104,7 +105,6 @@ __global__ void __launch_bounds__(kArThreads)
       reinterpret_cast<uint4*>(p.out + e0)[v] = o;
     }
   }
-  pdl_launch_dependents();
   // 5. The last CTA of the call advances the epoch for the next call.
   __syncthreads();
   if (tid == 0) {

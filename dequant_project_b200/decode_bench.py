@@ -208,8 +208,11 @@ def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = 
                           "frac": round(a / peaks["hbm_gbs"], 4),
                           "share_of_step": round(part["ms"] / ms, 3)}
     if tp1_err is not None:
-        line["tp1_check"] = {"max_rel_err_vs_tp1": tp1_err, "tolerance": 5e-3,
-                             "ok": tp1_err <= 5e-3}
+        # 32 random layers amplify the fp16 rounding differences of another
+        # summation order (partial sums per rank); the gloo tests bound the
+        # kernels' own arithmetic at 5e-3 on two layers.
+        line["tp1_check"] = {"max_rel_err_vs_tp1": tp1_err, "tolerance": 2e-2,
+                             "ok": tp1_err <= 2e-2}
     return line
 
 
@@ -288,7 +291,7 @@ def _parser() -> argparse.ArgumentParser:
                     help="load the packed model from this file (packed_io format)")
     ap.add_argument("--save-weights", default=None,
                     help="pack the model once, write it to this file and exit")
-    ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
+    ap.add_argument("--allreduce", choices=("peer", "fused", "nccl"), default="peer",
                     help="collective after the row-parallel layers (world > 1)")
     ap.add_argument("--gemv-path", type=int, default=0, choices=(0, 1),
                     help="dqg_set_gemv_path: 0 = per shape (default), 1 = no direct kernel")

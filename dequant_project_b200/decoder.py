@@ -205,7 +205,9 @@ class TPDecoder:
     from disk) supplies them already packed, so no rank quantizes anything.
     Each rank takes its shard of every full matrix. ``allreduce`` picks the
     collective after the row-parallel layers on CUDA ranks: ``"peer"`` (the
-    one-shot all-reduce over peer memory of ``peer_reduce``, the default) or
+    GEMV, then the one-shot all-reduce over peer memory of ``peer_reduce``;
+    the default), ``"fused"`` (one kernel: the row-parallel GEMV exchanging
+    its partial rows through peer memory, where the shape has a fused plan) or
     ``"nccl"`` (``torch.distributed.all_reduce``); CPU ranks always use the
     process group. ``close()`` releases the peer mappings."""
 
@@ -290,10 +292,11 @@ class TPDecoder:
         self._attn_ws = (ops.attention_workspace(batch, self.hq, self.hkv, self.capacity,
                                                  self.device)
                          if self.device.type == "cuda" else None)
-        if allreduce not in ("peer", "nccl"):
-            raise ValueError(f"allreduce must be 'peer' or 'nccl', got {allreduce!r}")
+        if allreduce not in ("peer", "fused", "nccl"):
+            raise ValueError(f"allreduce must be 'peer', 'fused' or 'nccl', got {allreduce!r}")
         self._peer = None
-        if world > 1 and allreduce == "peer" and self.device.type == "cuda":
+        self._fused = allreduce == "fused"
+        if world > 1 and allreduce != "nccl" and self.device.type == "cuda":
             from dequant_project_b200.peer_reduce import PeerAllReduce
             self._peer = PeerAllReduce(group, self.device, batch * cfg.hidden)
 
@@ -336,7 +339,7 @@ class TPDecoder:
         """A row-parallel layer: the fused GEMV + peer all-reduce on CUDA ranks
         with the peer collective (one kernel where the shape has a fused
         plan), else this rank's GEMV and the all-reduce."""
-        if self._peer is not None and self._linear is _default_linear:
+        if self._peer is not None and self._fused and self._linear is _default_linear:
             return self._peer.gemv(x, pw)
         return self._all_reduce(self._linear(x, pw))
 

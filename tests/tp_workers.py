@@ -221,7 +221,7 @@ def decoder_peer_vs_nccl(rank, world, port, queue):
         dev = torch.device("cuda", rank)
         tokens = torch.tensor([3, 4001], device=dev)
         outs = {}
-        for mode in ("peer", "nccl"):
+        for mode in ("peer", "fused", "nccl"):
             dec = TPDecoder(cfg, QuantConfig(4, 128, False), world=world, rank=rank, device=dev,
                             seed=5, batch=2, kv_len=100, allreduce=mode)
             eager = dec.step(tokens, 100).clone()
@@ -234,10 +234,12 @@ def decoder_peer_vs_nccl(rank, world, port, queue):
             if not torch.equal(rep, eager):
                 raise AssertionError(f"{mode}: graph replay differs from the eager step")
             outs[mode] = eager
-        a, b = outs["peer"].float(), outs["nccl"].float()
-        err = ((a - b).abs().max() / b.abs().max()).item()
-        if err > 5e-3:
-            raise AssertionError(f"peer vs nccl decoder logits differ by {err}")
+        b = outs["nccl"].float()
+        for mode in ("peer", "fused"):
+            a = outs[mode].float()
+            err = ((a - b).abs().max() / b.abs().max()).item()
+            if err > 5e-3:
+                raise AssertionError(f"{mode} vs nccl decoder logits differ by {err}")
         queue.put((rank, "ok", outs["peer"].cpu()))
         dist.barrier()
         dist.destroy_process_group()
