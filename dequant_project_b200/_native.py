@@ -16,6 +16,25 @@ LIB_PATH = Path(__file__).resolve().parent / "libdequant_b200.so"
 _lib = None
 
 
+class L2Spans(ctypes.Structure):
+    """``dqg_l2_spans``: up to 8 device byte ranges to bring into L2."""
+    _fields_ = [("ptr", ctypes.c_void_p * 8), ("bytes", ctypes.c_uint64 * 8),
+                ("n", ctypes.c_int32)]
+
+    @classmethod
+    def of(cls, ranges) -> "L2Spans":
+        """From ``(pointer, bytes)`` pairs (at most 8)."""
+        ranges = [(p, b) for p, b in ranges if b > 0]
+        if len(ranges) > 8:
+            raise ValueError(f"at most 8 prefetch ranges, got {len(ranges)}")
+        s = cls()
+        for i, (p, b) in enumerate(ranges):
+            s.ptr[i] = p
+            s.bytes[i] = b
+        s.n = len(ranges)
+        return s
+
+
 def lib() -> ctypes.CDLL:
     """Load (once) and return the C-ABI library."""
     global _lib
@@ -40,11 +59,13 @@ def lib() -> ctypes.CDLL:
     h.dqg_device_status.restype = i32
     h.dqg_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
     h.dqg_add_rms_norm.restype = i32
-    h.dqg_add_rms_norm.argtypes = [vp, vp, vp, vp, i64, i64, ctypes.c_float, vp]
+    spans = ctypes.POINTER(L2Spans)
+    h.dqg_add_rms_norm.argtypes = [vp, vp, vp, vp, i64, i64, ctypes.c_float, spans, vp]
     h.dqg_rope_kv_append.restype = i32
-    h.dqg_rope_kv_append.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
+    h.dqg_rope_kv_append.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, spans,
+                                     vp]
     h.dqg_silu_mul.restype = i32
-    h.dqg_silu_mul.argtypes = [vp, vp, i64, i64, vp]
+    h.dqg_silu_mul.argtypes = [vp, vp, i64, i64, spans, vp]
     h.dqg_set_weight_prefetch.restype = i32
     h.dqg_set_weight_prefetch.argtypes = [i32]
     h.dqg_set_gemv_path.restype = i32

@@ -53,6 +53,55 @@ int check_device_ptr(const void* p, int dev, const char* name) {
   return DQG_OK;
 }
 
+// The driver's cuMemGetAddressRange, looked up at run time (the library does
+// not link the driver library), or null where the driver does not offer it.
+using AddrRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn addr_range_fn() {
+  static const AddrRangeFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<AddrRangeFn>(nullptr);
+    }
+    return reinterpret_cast<AddrRangeFn>(f);
+  }();
+  return fn;
+}
+
+// L2 prefetch ranges of a decode op, checked (each inside one device
+// allocation of `dev`) and trimmed to 16-byte aligned starts and sizes.
+int prepare_prefetch(const dqg_l2_spans* in, int dev, dqg::L2Spans* out) {
+  std::memset(out, 0, sizeof(*out));
+  if (in == nullptr || in->n == 0) return DQG_OK;
+  if (in->n < 0 || in->n > 8)
+    return fail(DQG_ERR_INVALID, "prefetch.n must be in [0, 8], got %d", static_cast<int>(in->n));
+  const AddrRangeFn range = addr_range_fn();
+  if (range == nullptr) return fail(DQG_ERR_UNSUPPORTED, "the driver has no cuMemGetAddressRange");
+  for (int i = 0; i < in->n; ++i) {
+    const uint64_t b = in->bytes[i];
+    if (b == 0) continue;
+    int rc = check_device_ptr(in->ptr[i], dev, "prefetch range");
+    if (rc) return rc;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    const uintptr_t p = reinterpret_cast<uintptr_t>(in->ptr[i]);
+    if (range(&base, &size, static_cast<CUdeviceptr>(p)) != CUDA_SUCCESS)
+      return fail(DQG_ERR_INVALID, "prefetch range %d is not inside a device allocation", i);
+    if (p + b > static_cast<uintptr_t>(base) + size)
+      return fail(DQG_ERR_INVALID, "prefetch range %d runs past the end of its allocation", i);
+    const uintptr_t a = (p + 15) & ~static_cast<uintptr_t>(15);
+    if (a - p >= b) continue;
+    const uint64_t len = (b - (a - p)) & ~static_cast<uint64_t>(15);
+    if (len == 0) continue;
+    out->ptr[out->n] = reinterpret_cast<const uint8_t*>(a);
+    out->bytes[out->n] = len;
+    ++out->n;
+  }
+  return DQG_OK;
+}
+
 // Pointer-kind checks (cudaPointerGetAttributes on every operand) cost a few
 // microseconds per call, which is comparable to a small GEMV; they run only
 // when DQG_CHECK_POINTERS is set to a non-empty value other than "0". The
@@ -325,7 +374,7 @@ int dqg_dequantize(const int32_t* qweight, const void* scales, const void* zeros
 }
 
 int dqg_add_rms_norm(void* h, const void* delta, const void* weight, void* y, int64_t M,
-                     int64_t H, float eps, void* stream) {
+                     int64_t H, float eps, const dqg_l2_spans* prefetch, void* stream) {
   if (M < 1 || M > 65535) return fail(DQG_ERR_INVALID, "M must be in [1, 65535], got %lld", (long long)M);
   if (H < 8 || H % 8 != 0 || H > (1 << 24))
     return fail(DQG_ERR_INVALID, "H must be a positive multiple of 8, got %lld", (long long)H);
@@ -342,8 +391,11 @@ int dqg_add_rms_norm(void* h, const void* delta, const void* weight, void* y, in
     if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16)
       return fail(DQG_ERR_INVALID, "%s must be 16-byte aligned", names[i]);
   }
+  dqg::L2Spans pf;
+  int rc = prepare_prefetch(prefetch, dev, &pf);
+  if (rc) return rc;
   e = dqg::launch_add_rms_norm(h, delta, weight, y, static_cast<int>(M), static_cast<int>(H), eps,
-                               static_cast<cudaStream_t>(stream));
+                               pf, sm_count(dev), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "add_rms_norm launch");
   return ok();
 }
@@ -351,7 +403,7 @@ int dqg_add_rms_norm(void* h, const void* delta, const void* weight, void* y, in
 int dqg_rope_kv_append(const void* qkv, const float* cos_row, const float* sin_row, void* q_out,
                        void* k_cache, void* v_cache, int64_t M, int64_t n_q_heads,
                        int64_t n_kv_heads, int64_t head_dim, int64_t pos, int64_t capacity,
-                       void* stream) {
+                       const dqg_l2_spans* prefetch, void* stream) {
   if (M < 1 || M > 65535) return fail(DQG_ERR_INVALID, "M must be in [1, 65535], got %lld", (long long)M);
   if (n_q_heads < 1 || n_kv_heads < 1 || n_q_heads + n_kv_heads > 65535)
     return fail(DQG_ERR_INVALID, "head counts out of range (%lld query, %lld KV)",
@@ -373,16 +425,20 @@ int dqg_rope_kv_append(const void* qkv, const float* cos_row, const float* sin_r
     int rc = check_device_ptr(ptrs[i], dev, names[i]);
     if (rc) return rc;
   }
+  dqg::L2Spans pf;
+  int rc = prepare_prefetch(prefetch, dev, &pf);
+  if (rc) return rc;
   e = dqg::launch_rope_kv_append(qkv, cos_row, sin_row, q_out, k_cache, v_cache,
                                  static_cast<int>(M), static_cast<int>(n_q_heads),
                                  static_cast<int>(n_kv_heads), static_cast<int>(head_dim),
-                                 static_cast<int>(pos), static_cast<int>(capacity),
-                                 static_cast<cudaStream_t>(stream));
+                                 static_cast<int>(pos), static_cast<int>(capacity), pf,
+                                 sm_count(dev), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rope_kv_append launch");
   return ok();
 }
 
-int dqg_silu_mul(const void* gate_up, void* out, int64_t M, int64_t I, void* stream) {
+int dqg_silu_mul(const void* gate_up, void* out, int64_t M, int64_t I,
+                 const dqg_l2_spans* prefetch, void* stream) {
   if (M < 1 || I < 1 || M * I > (int64_t(1) << 40))
     return fail(DQG_ERR_INVALID, "M and I must be positive (got %lld, %lld)", (long long)M,
                 (long long)I);
@@ -394,8 +450,11 @@ int dqg_silu_mul(const void* gate_up, void* out, int64_t M, int64_t I, void* str
   if (rc) return rc;
   rc = check_device_ptr(out, dev, "out");
   if (rc) return rc;
-  e = dqg::launch_silu_mul(gate_up, out, static_cast<int>(M), static_cast<int>(I),
-                           static_cast<cudaStream_t>(stream));
+  dqg::L2Spans pf;
+  rc = prepare_prefetch(prefetch, dev, &pf);
+  if (rc) return rc;
+  e = dqg::launch_silu_mul(gate_up, out, static_cast<int>(M), static_cast<int>(I), pf,
+                           sm_count(dev), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "silu_mul launch");
   return ok();
 }

@@ -9,6 +9,14 @@
 // the next grid launch: a GEMV that follows can be scheduled and run its own
 // set-up while one of these runs, and one of these can be scheduled while a
 // GEMV runs, so their launch latencies overlap instead of adding up.
+//
+// Each can also carry byte ranges of a later GEMV's packed weights to bring
+// into L2 (bulk L2 prefetches issued before the dependency wait). The decoder
+// step leaves HBM idle while these ops, the attention and each GEMV's start
+// and end run; prefetching the next weights there lets that GEMV read them
+// from L2. The grid is widened to the SM count so every SM's copy engine
+// issues a share; the extra CTAs only prefetch and exit (the op's own CTAs
+// still wait for the previous grid, so the chain of dependencies holds).
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -20,18 +28,40 @@ namespace dqg {
 namespace {
 
 constexpr int kNormThreads = 256;
+constexpr uint64_t kPrefetchPiece = 16384;  // bytes per bulk L2 prefetch
+
+// This CTA's share of the prefetch ranges: piece j of a range goes to CTA
+// j % ncta (so that every SM's copy engine takes part), thread j / ncta.
+// Fire and forget: nothing waits for these, and the op's own work does not
+// depend on them.
+__device__ __forceinline__ void l2_prefetch_share(const L2Spans& pf, int cta, int ncta) {
+  const uint64_t rank = static_cast<uint64_t>(threadIdx.x) * ncta + cta;
+  const uint64_t nt = static_cast<uint64_t>(ncta) * blockDim.x;
+  for (int i = 0; i < pf.n; ++i) {
+    const uint64_t n = pf.bytes[i];
+    for (uint64_t off = rank * kPrefetchPiece; off < n; off += nt * kPrefetchPiece) {
+      const uint32_t len = static_cast<uint32_t>(n - off < kPrefetchPiece ? n - off : kPrefetchPiece);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.ptr[i] + off), "r"(len)
+                   : "memory");
+    }
+  }
+}
 
 __device__ __forceinline__ float h2f(__half v) { return __half2float(v); }
 
 // h[m] = fp16(h[m] + delta[m]) (when delta is given), then
 // y[m] = fp16((h * rsqrt(mean(h^2) + eps)) * w), in fp32 with the two products
 // rounded one at a time as torch evaluates them.
+// CTAs m >= M only issue their share of the prefetch.
 __global__ void __launch_bounds__(kNormThreads)
     add_rms_norm_kernel(__half* __restrict__ h, const __half* __restrict__ delta,
-                        const __half* __restrict__ w, __half* __restrict__ y, int H, float eps) {
+                        const __half* __restrict__ w, __half* __restrict__ y, int M, int H,
+                        float eps, const __grid_constant__ L2Spans pf) {
+  if (pf.n) l2_prefetch_share(pf, blockIdx.x, gridDim.x);
+  const int m = blockIdx.x;
+  if (m >= M) return;
   pdl_wait_prior_grid();
   pdl_launch_dependents();
-  const int m = blockIdx.x;
   __half* hr = h + static_cast<int64_t>(m) * H;
   const __half* dr = delta ? delta + static_cast<int64_t>(m) * H : nullptr;
   __half* yr = y + static_cast<int64_t>(m) * H;
@@ -82,10 +112,16 @@ __global__ void __launch_bounds__(kNormThreads)
 //   out[i]     = x[i] * cos[i]         + (-x[i + D/2]) * sin[i]
 //   out[i+D/2] = x[i + D/2] * cos[i+D/2] + x[i] * sin[i + D/2]
 // each product and the sum rounded in fp32, then to fp16.
+// Grid (M, hq + hkv, z): CTAs with blockIdx.z > 0 only prefetch.
 __global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const float* __restrict__ cosv,
                                       const float* __restrict__ sinv, __half* __restrict__ q_out,
                                       __half* __restrict__ kc, __half* __restrict__ vc, int hq,
-                                      int hkv, int D, int pos, int cap) {
+                                      int hkv, int D, int pos, int cap,
+                                      const __grid_constant__ L2Spans pf) {
+  if (pf.n)
+    l2_prefetch_share(pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                      gridDim.x * gridDim.y * gridDim.z);
+  if (blockIdx.z > 0) return;
   pdl_wait_prior_grid();
   pdl_launch_dependents();
   const int m = blockIdx.x;
@@ -118,7 +154,8 @@ __global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const floa
 // out[m, i] = fp16(silu(g) * u), g = gu[m, i], u = gu[m, I + i],
 // silu(g) = g / (1 + exp(-g)) in fp32.
 __global__ void silu_mul_kernel(const __half* __restrict__ gu, __half* __restrict__ out, int I,
-                                int64_t total) {
+                                int64_t total, const __grid_constant__ L2Spans pf) {
+  if (pf.n) l2_prefetch_share(pf, blockIdx.x, gridDim.x);
   pdl_wait_prior_grid();
   pdl_launch_dependents();
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
@@ -152,28 +189,35 @@ cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, int threads, cudaStre
 }
 
 cudaError_t launch_add_rms_norm(void* h, const void* delta, const void* w, void* y, int M, int H,
-                                float eps, cudaStream_t stream) {
-  return launch_pdl(add_rms_norm_kernel, dim3(M), kNormThreads, stream, static_cast<__half*>(h),
+                                float eps, const L2Spans& pf, int num_sms, cudaStream_t stream) {
+  const int grid = pf.n && M < num_sms ? num_sms : M;
+  return launch_pdl(add_rms_norm_kernel, dim3(grid), kNormThreads, stream, static_cast<__half*>(h),
                     static_cast<const __half*>(delta), static_cast<const __half*>(w),
-                    static_cast<__half*>(y), H, eps);
+                    static_cast<__half*>(y), M, H, eps, pf);
 }
 
 cudaError_t launch_rope_kv_append(const void* qkv, const float* cosv, const float* sinv,
                                   void* q_out, void* kc, void* vc, int M, int hq, int hkv, int D,
-                                  int pos, int cap, cudaStream_t stream) {
+                                  int pos, int cap, const L2Spans& pf, int num_sms,
+                                  cudaStream_t stream) {
   const int threads = D / 2 < 32 ? 32 : (D / 2 > 256 ? 256 : D / 2);
-  return launch_pdl(rope_kv_append_kernel, dim3(M, hq + hkv), threads, stream,
+  const int base = M * (hq + hkv);
+  const int z = pf.n && base < num_sms ? (num_sms + base - 1) / base : 1;
+  return launch_pdl(rope_kv_append_kernel, dim3(M, hq + hkv, z), threads, stream,
                     static_cast<const __half*>(qkv), cosv, sinv, static_cast<__half*>(q_out),
-                    static_cast<__half*>(kc), static_cast<__half*>(vc), hq, hkv, D, pos, cap);
+                    static_cast<__half*>(kc), static_cast<__half*>(vc), hq, hkv, D, pos, cap, pf);
 }
 
-cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, cudaStream_t stream) {
+cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, const L2Spans& pf,
+                            int num_sms, cudaStream_t stream) {
   const int64_t total = static_cast<int64_t>(M) * I;
   const int threads = 256;
+  const int sms = num_sms > 0 ? num_sms : 148;
   int64_t blocks = (total + threads - 1) / threads;
-  if (blocks > 4 * 148) blocks = 4 * 148;
+  if (blocks > 4 * sms) blocks = 4 * sms;
+  if (pf.n && blocks < sms) blocks = sms;
   return launch_pdl(silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), threads, stream,
-                    static_cast<const __half*>(gu), static_cast<__half*>(out), I, total);
+                    static_cast<const __half*>(gu), static_cast<__half*>(out), I, total, pf);
 }
 
 }  // namespace dqg

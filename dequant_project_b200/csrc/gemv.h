@@ -265,11 +265,20 @@ cudaError_t read_status_direct_b8(uint32_t* status, bool reset);
 cudaError_t launch_add_one(const float* x, float* out, int64_t n, cudaStream_t stream);
 
 // Decoder-step element-wise kernels (decode_ops.cu).
+// Bulk L2 prefetch ranges carried by the decode ops (16-byte aligned starts
+// and sizes, normalised by the host).
+struct L2Spans {
+  const uint8_t* ptr[8];
+  uint64_t bytes[8];
+  int n;
+};
 cudaError_t launch_add_rms_norm(void* h, const void* delta, const void* w, void* y, int M, int H,
-                                float eps, cudaStream_t stream);
+                                float eps, const L2Spans& pf, int num_sms, cudaStream_t stream);
 cudaError_t launch_rope_kv_append(const void* qkv, const float* cosv, const float* sinv,
                                   void* q_out, void* kc, void* vc, int M, int hq, int hkv, int D,
-                                  int pos, int cap, cudaStream_t stream);
-cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, cudaStream_t stream);
+                                  int pos, int cap, const L2Spans& pf, int num_sms,
+                                  cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* gu, void* out, int M, int I, const L2Spans& pf,
+                            int num_sms, cudaStream_t stream);
 
 }  // namespace dqg

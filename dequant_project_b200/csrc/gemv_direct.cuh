@@ -149,14 +149,19 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
   const int c = lane & 3;
   const int G = p.G;
   const int Gp = p.Gp;
-  const int upt = Gp / GS;  // units per tile
   const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
   const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
   const int T = (row_end - row_begin + kTile - 1) / kTile;
-  const int U = T * upt;
-  const int u_lo = static_cast<int>(static_cast<int64_t>(U) * warp / kDirectNW);
-  const int u_hi = static_cast<int>(static_cast<int64_t>(U) * (warp + 1) / kDirectNW);
-  const int s_lo = u_lo * GS, s_hi = u_hi * GS;
+  // Warps split the CTA's steps evenly (to within one step): live steps are
+  // [l_lo, l_hi). The loop runs over whole units around them, [s_lo, s_hi);
+  // the steps outside the live range load and compute nothing, and their
+  // group slots are left out of the unit epilogue.
+  const int S_all = T * Gp;
+  const int l_lo = static_cast<int>(static_cast<int64_t>(S_all) * warp / kDirectNW);
+  const int l_hi = static_cast<int>(static_cast<int64_t>(S_all) * (warp + 1) / kDirectNW);
+  const int s_lo = l_lo / GS * GS;
+  const int s_hi = l_hi > l_lo ? (l_hi + GS - 1) / GS * GS : s_lo;
+  auto live_step = [&](int s) { return s >= l_lo && s < l_hi; };
   const int64_t row_bytes = static_cast<int64_t>(p.K) * BITS / 8;
   const uint8_t* qw = reinterpret_cast<const uint8_t*>(p.qw) + c * (WPL * 4);
 
@@ -183,15 +188,40 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
     return ring_base + static_cast<uint32_t>(((j * 2 + half) * 32 + lane) * kLaneBytes);
   };
   uint32_t meta[MU][NMETA];
-  auto load_step = [&](int j, Cursor q, bool live) {
-    const int ra = row_begin + q.t * kTile + gid;
-    const bool ok = live && q.g < G;
-    const uint8_t* src = qw + static_cast<int64_t>(q.g) * kRowStepBytes;
-    const bool oka = ok && ra < row_end, okb = ok && ra + 8 < row_end;
-    cp_async<kLaneBytes>(slot_addr(j, 0), oka ? src + ra * row_bytes : qw,
-                         oka ? kLaneBytes : 0u);
-    cp_async<kLaneBytes>(slot_addr(j, 1), okb ? src + (ra + 8) * row_bytes : qw,
-                         okb ? kLaneBytes : 0u);
+  // The copy cursor: step s, its tile and group, and this lane's source
+  // addresses in rows gid and gid + 8 of the tile, advanced by one group's
+  // bytes per step (recomputed only when the tile changes).
+  struct LoadCur {
+    int s, t, g;
+    bool oka, okb;
+    const uint8_t* pa;
+    const uint8_t* pb;
+  };
+  auto lc_set = [&](LoadCur& L, int s) {
+    L.s = s;
+    L.t = s / Gp;
+    L.g = s - L.t * Gp;
+    const int ra = row_begin + L.t * kTile + gid;
+    L.oka = ra < row_end;
+    L.okb = ra + 8 < row_end;
+    const uint8_t* g0 = qw + static_cast<int64_t>(L.g) * kRowStepBytes;
+    L.pa = g0 + (L.oka ? ra : row_begin) * row_bytes;
+    L.pb = g0 + (L.okb ? ra + 8 : row_begin) * row_bytes;
+  };
+  auto lc_next = [&](LoadCur& L) {
+    ++L.s;
+    L.pa += kRowStepBytes;
+    L.pb += kRowStepBytes;
+    if (++L.g == Gp) lc_set(L, L.s);
+  };
+  // Copies of the cursor's step into the ring slot at byte address `slot`
+  // (zero fill where the step is outside this warp's live range, past the
+  // last group or past the CTA's rows), one commit group per step.
+  auto issue = [&](uint32_t slot, const LoadCur& L) {
+    const bool ok = live_step(L.s) && L.g < G;
+    const bool oka = ok && L.oka, okb = ok && L.okb;
+    cp_async<kLaneBytes>(slot, oka ? L.pa : qw, oka ? kLaneBytes : 0u);
+    cp_async<kLaneBytes>(slot + 32 * kLaneBytes, okb ? L.pb : qw, okb ? kLaneBytes : 0u);
     cp_async_commit();
   };
   // Scales (and zero-points) of the unit that starts at cursor q: for
@@ -221,15 +251,13 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
   // Issue the first ring: weights and metadata are not written by the
   // previous grid (with p.prefetch), so this runs before its dependency wait.
   if (!p.prefetch) pdl_wait_prior_grid();
-  {
-    Cursor q = cursor_at(s_lo);
+  LoadCur lq;
+  lc_set(lq, s_lo);
 #pragma unroll
-    for (int j = 0; j < R; ++j) {
-      const bool live = s_lo + j < s_hi;
-      if (j % GS == 0) load_meta(meta[j / GS], q, live);
-      load_step(j, q, live);
-      advance(q);
-    }
+  for (int j = 0; j < R; ++j) {
+    if (j % GS == 0) load_meta(meta[j / GS], Cursor{lq.t, lq.g}, s_lo + j < s_hi);
+    issue(slot_addr(j, 0), lq);
+    lc_next(lq);
   }
   if (threadIdx.x == 0) pdl_launch_dependents();
 
@@ -337,7 +365,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
 
   // Unit epilogue: scales and zero-points of the unit's groups (from g0)
   // applied in fp32 to the chains' sums, added into acc.
-  auto epilogue = [&](const uint32_t* md, int g0) {
+  auto epilogue = [&](const uint32_t* md, int g0, int tile_step) {
     float P[4];
     stream::combine<NCH>(D, P);
 #pragma unroll
@@ -350,7 +378,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
       const int slot = (2 * c) / MP;
       const int xr0 = 2 * c - slot * MP;
       const int g = g0 + slot;
-      const bool gok = g < G;
+      const bool gok = g < G && live_step(tile_step + g);
       ev[0] = ev[2] = gok && xr0 < p.M;
       ev[1] = ev[3] = gok && xr0 + 1 < p.M;
       sv[0] = sv[1] = h2f(md[0]);
@@ -367,7 +395,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
       for (int e = 0; e < 4; ++e) {
         const int gi = e & 1, h = e >> 1;
         const int g = g0 + 2 * c + gi;
-        ev[e] = g < G;
+        ev[e] = g < G && live_step(tile_step + g);
         sv[e] = h2f(md[gi * 2 + h]);
         if constexpr (!SYM) {
           zv[e] = h2f(md[4 + gi * 2 + h]);
@@ -405,7 +433,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
       for (int e = 0; e < 4; ++e) a[e] += __shfl_xor_sync(0xffffffffu, a[e], 2);
     }
     constexpr int cmask = MP <= 2 ? 3 : (MP == 4 ? 2 : 0);
-    const bool whole = t * upt >= u_lo && (t + 1) * upt <= u_hi;
+    const bool whole = t * Gp >= l_lo && (t + 1) * Gp <= l_hi;
     const int r0 = row_begin + t * kTile;
     const int slot = t == first_tile ? 0 : 1;
     float* rs = red + slot * (kTile * 8);
@@ -430,54 +458,113 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
 
   if (lane == 0) tiles[warp * 2] = tiles[warp * 2 + 1] = -1;
   __syncwarp();
-  Cursor cq = cursor_at(s_lo);      // the step computed
-  Cursor lq = cursor_at(s_lo + R);  // the step loaded into the slot just consumed
-  Cursor mq = lq;                   // start of the unit whose metadata is loaded next
-  for (int base = s_lo; base < s_hi; base += R) {
+  const uint32_t smem_base = smem_u32(smem);
+  constexpr uint32_t kSlotBytes = 64 * kLaneBytes;  // one step's ring slot, both row halves
+  if constexpr (GS >= 4) {
+    // Batch of at most two activation rows (four or eight group slots): a
+    // unit's steps are unrolled with the ring slot of the unit computed
+    // once, and each unit's scales/zero-points are loaded one unit ahead
+    // (the unit after next, into `mnxt`, while this one is computed).
+    uint32_t mnxt[NMETA];
+    if constexpr (MU >= 2) {
 #pragma unroll
-    for (int j = 0; j < R; ++j) {
-      const int s = base + j;
-      if (s < s_hi) {
-        if (j % GS == 0) mq = lq;
-        cp_async_wait<R - 1>();  // step s has landed (this lane's copies)
-        if (cq.g < G) {
+      for (int i = 0; i < NMETA; ++i) mnxt[i] = meta[1][i];
+    } else {
+      load_meta(mnxt, cursor_at(s_lo + GS), s_lo + GS < s_hi);
+    }
+    int t = s_lo / Gp, g0 = s_lo - (s_lo / Gp) * Gp;
+    int ru = 0;  // ring position of the unit, in units
+    for (int u0 = s_lo; u0 < s_hi; u0 += GS) {
+      const uint32_t ring_u = ring_base + lane * kLaneBytes + ru * GS * kSlotBytes;
+#pragma unroll
+      for (int jj = 0; jj < GS; ++jj) {
+        const uint32_t sa = ring_u + jj * kSlotBytes;
+        cp_async_wait<R - 1>();  // step u0 + jj has landed (this lane's copies)
+        if (g0 + jj < G && live_step(u0 + jj)) {
           uint32_t w[2 * WPL];
-          lds<kLaneBytes>(smem + (slot_addr(j, 0) - smem_u32(smem)), w);
-          lds<kLaneBytes>(smem + (slot_addr(j, 1) - smem_u32(smem)), w + WPL);
-          const bool live = x_ok && my_slot == j % GS;
-          mma_regs<BITS, WPL>(w, w + WPL, live ? xrow_base + cq.g * STEP_XB : zero_base, D);
+          lds<kLaneBytes>(smem + (sa - smem_base), w);
+          lds<kLaneBytes>(smem + (sa + 32 * kLaneBytes - smem_base), w + WPL);
+          const bool live = x_ok && my_slot == jj;
+          mma_regs<BITS, WPL>(w, w + WPL, live ? xrow_base + (g0 + jj) * STEP_XB : zero_base, D);
         }
-        load_step(j, lq, s + R < s_hi);
-        if (j % GS == GS - 1) {
-          epilogue(meta[j / GS], cq.g - (GS - 1));
-          load_meta(meta[j / GS], mq, s + 1 - GS + R < s_hi);
-          if (cq.g == Gp - 1 || s == s_hi - 1) tile_flush(cq.t);
+        issue(sa, lq);  // step u0 + jj + R into the slot just read
+        lc_next(lq);
+      }
+      epilogue(meta[0], g0, t * Gp);
+#pragma unroll
+      for (int i = 0; i < NMETA; ++i) meta[0][i] = mnxt[i];
+      const int un = u0 + 2 * GS;
+      if (un < s_hi) load_meta(mnxt, cursor_at(un), true);
+      if (g0 + GS == Gp || u0 + GS == s_hi) tile_flush(t);
+      g0 += GS;
+      if (g0 == Gp) {
+        g0 = 0;
+        ++t;
+      }
+      ru = ru + 1 == MU ? 0 : ru + 1;
+    }
+  } else {
+    Cursor cq = cursor_at(s_lo);      // the step computed
+    Cursor mq = cursor_at(s_lo + R);  // start of the unit whose metadata is loaded next
+    for (int base = s_lo; base < s_hi; base += R) {
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const int s = base + j;
+        if (s < s_hi) {
+          cp_async_wait<R - 1>();  // step s has landed (this lane's copies)
+          if (cq.g < G && live_step(s)) {
+            uint32_t w[2 * WPL];
+            lds<kLaneBytes>(smem + (slot_addr(j, 0) - smem_base), w);
+            lds<kLaneBytes>(smem + (slot_addr(j, 1) - smem_base), w + WPL);
+            const bool live = x_ok && my_slot == j % GS;
+            mma_regs<BITS, WPL>(w, w + WPL, live ? xrow_base + cq.g * STEP_XB : zero_base, D);
+          }
+          issue(slot_addr(j, 0), lq);
+          lc_next(lq);
+          if (j % GS == GS - 1) {
+            epilogue(meta[j / GS], cq.g - (GS - 1), cq.t * Gp);
+            load_meta(meta[j / GS], mq, s + 1 - GS + R < s_hi);
+#pragma unroll
+            for (int k2 = 0; k2 < GS; ++k2) advance(mq);
+            if (cq.g == Gp - 1 || s == s_hi - 1) tile_flush(cq.t);
+          }
+          advance(cq);
         }
-        advance(cq);
-        advance(lq);
       }
     }
   }
 
   // Tiles shared between warps: the lowest warp holding a tile adds every
-  // holder's partial in warp order and writes y.
+  // holder's partial in warp order and writes y. The holder table is read
+  // into registers once and the loops over warps are unrolled, so that the
+  // partials' shared-memory loads are independent of one another.
   __syncthreads();
+  int tl[2 * kDirectNW];
+#pragma unroll
+  for (int i = 0; i < 2 * kDirectNW; ++i) tl[i] = tiles[i];
+  const float* red_all = reinterpret_cast<const float*>(smem + p.off_red);
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
     const int t = tiles[warp * 2 + slot];
     if (t < 0) continue;
     bool lowest = true;
-    for (int w = 0; w < warp; ++w) lowest = lowest && tiles[w * 2] != t && tiles[w * 2 + 1] != t;
+#pragma unroll
+    for (int w = 0; w < kDirectNW; ++w)
+      if (w < warp) lowest = lowest && tl[2 * w] != t && tl[2 * w + 1] != t;
     if (!lowest) continue;
     const int r0 = row_begin + t * kTile;
     for (int idx = lane; idx < kTile * p.M; idx += 32) {
       const int row = idx / p.M, xrow = idx - (idx / p.M) * p.M;
-      float sum = 0.f;
-      for (int w = warp; w < kDirectNW; ++w) {
-        const float* rw = reinterpret_cast<const float*>(smem + p.off_red) + w * (2 * kTile * 8);
-        if (tiles[w * 2] == t) sum += rw[row * 8 + xrow];
-        if (tiles[w * 2 + 1] == t) sum += rw[kTile * 8 + row * 8 + xrow];
+      float part[2 * kDirectNW];
+#pragma unroll
+      for (int w = 0; w < kDirectNW; ++w) {
+        const float* rw = red_all + w * (2 * kTile * 8) + row * 8 + xrow;
+        part[2 * w] = w >= warp && tl[2 * w] == t ? rw[0] : 0.f;
+        part[2 * w + 1] = w >= warp && tl[2 * w + 1] == t ? rw[kTile * 8] : 0.f;
       }
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 2 * kDirectNW; ++i) sum += part[i];
       if (r0 + row < row_end) store_out(xrow, r0 + row, sum);
     }
   }

@@ -105,6 +105,19 @@ def attention_only(dec, dev, pos: int) -> tuple:
     return _capture(run, dev), nbytes
 
 
+def allreduce_only(dec, dev) -> tuple:
+    """(graph, launches) of the step's all-reduces alone: two per layer over
+    [batch, hidden] fp16, through the decoder's collective (world > 1)."""
+    t = torch.randn(dec.batch, dec.cfg.hidden, device=dev, dtype=torch.float16)
+    n = 2 * dec.cfg.n_layers
+
+    def run():
+        for _ in range(n):
+            dec._all_reduce(t)
+
+    return _capture(run, dev), n
+
+
 def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = True,
             e2e: bool = True, check_tp1: bool = False) -> dict | None:
     """Build this rank's shard, capture and time the step (see the module
@@ -122,7 +135,8 @@ def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = 
     cfg, q, weights = model_source(args, dev)
     dec = D.TPDecoder(cfg, q, world=world, rank=rank, device=dev, seed=args.seed,
                       batch=args.batch, kv_len=args.kv_len, weights=weights,
-                      allreduce=getattr(args, "allreduce", "peer"))
+                      allreduce=getattr(args, "allreduce", "peer"),
+                      l2_prefetch=getattr(args, "l2_prefetch", False))
     torch.cuda.synchronize(dev)
     gr = D.DecodeGraph(dec, args.kv_len)
     gr.tokens.copy_(torch.arange(args.batch, device=dev) * 7919 % cfg.vocab)
@@ -147,7 +161,7 @@ def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = 
                    "tokens_per_s": round(args.batch / (ms_e2e * 1e-3), 2),
                    "h2d_bytes_per_step": tok_host.numel() * 8,
                    "d2h_bytes_per_step": logit_host.numel() * 2}
-    gemv_part = attn_part = None
+    gemv_part = attn_part = ar_part = None
     if parts:
         g_gemv, launches, gbytes = gemv_only(dec, dev)
         ms_g = _time_graph(g_gemv.replay, args.steps, args.warmup, dev, dist)
@@ -158,6 +172,12 @@ def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = 
             ms_a = _time_graph(g_att.replay, args.steps, args.warmup, dev, dist)
             g_att.reset()
             attn_part = {"ms": ms_a, "launches": cfg.n_layers, "bytes": abytes}
+        if world > 1:
+            g_ar, n_ar = allreduce_only(dec, dev)
+            ms_r = _time_graph(g_ar.replay, args.steps, args.warmup, dev, dist)
+            g_ar.reset()
+            ar_part = {"ms": ms_r, "launches": n_ar,
+                       "bytes": n_ar * args.batch * cfg.hidden * 2}
     by = dec.step_bytes(args.kv_len)
     gr.release()
     dec.close()
@@ -189,7 +209,8 @@ def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = 
                    "kv_len": args.kv_len, "bits": q.bits,
                    "group_size": q.group_size or "per-channel",
                    "symmetric": q.symmetric, "lm_head": "packed, column-parallel",
-                   "allreduce": getattr(args, "allreduce", "peer") if world > 1 else None},
+                   "allreduce": getattr(args, "allreduce", "peer") if world > 1 else None,
+                   "l2_prefetch": getattr(args, "l2_prefetch", False)},
         "data": "synthetic (random-init N(0,0.02) weights, N(0,1) fp16 KV cache)",
         "bytes_per_rank": by,
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
@@ -207,6 +228,12 @@ def measure(args, dist, rank: int, world: int, dev: torch.device, parts: bool = 
                           "bytes_per_step": part["bytes"], "achieved_gbs": round(a, 1),
                           "frac": round(a / peaks["hbm_gbs"], 4),
                           "share_of_step": round(part["ms"] / ms, 3)}
+    if ar_part is not None:
+        line["allreduce"] = {"ms_per_step": round(ar_part["ms"], 4),
+                             "launches": ar_part["launches"],
+                             "us_per_launch": round(ar_part["ms"] * 1e3 / ar_part["launches"], 3),
+                             "bytes_per_launch": ar_part["bytes"] // ar_part["launches"],
+                             "share_of_step": round(ar_part["ms"] / ms, 3)}
     if tp1_err is not None:
         # 32 random layers amplify the fp16 rounding differences of another
         # summation order (partial sums per rank); the gloo tests bound the
@@ -291,6 +318,8 @@ def _parser() -> argparse.ArgumentParser:
                     help="load the packed model from this file (packed_io format)")
     ap.add_argument("--save-weights", default=None,
                     help="pack the model once, write it to this file and exit")
+    ap.add_argument("--l2-prefetch", action="store_true",
+                    help="L2 prefetch of later GEMVs' weights in the element-wise ops")
     ap.add_argument("--allreduce", choices=("peer", "fused", "nccl"), default="peer",
                     help="collective after the row-parallel layers (world > 1)")
     ap.add_argument("--gemv-path", type=int, default=0, choices=(0, 1),

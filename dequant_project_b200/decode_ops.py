@@ -22,10 +22,27 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def l2_spans(weights) -> "_native.L2Spans | None":
+    """The packed tensors of ``weights`` (PackedWeight objects) as L2 prefetch
+    ranges for a decode op, or None when there are none."""
+    ranges = []
+    for pw in weights:
+        for t in (pw.qweight, pw.scales, pw.zeros):
+            if t is not None and t.is_cuda:
+                ranges.append((t.data_ptr(), t.numel() * t.element_size()))
+    return _native.L2Spans.of(ranges) if ranges else None
+
+
+def _spans_arg(prefetch):
+    import ctypes
+    return None if prefetch is None else ctypes.byref(prefetch)
+
+
 def add_rms_norm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor,
-                 eps: float) -> torch.Tensor:
+                 eps: float, prefetch=None) -> torch.Tensor:
     """If ``delta`` is given, ``h += delta`` in place (fp16); returns
-    RMSNorm(h) * weight as fp16 [M, H] (fp32 math)."""
+    RMSNorm(h) * weight as fp16 [M, H] (fp32 math). ``prefetch`` (from
+    ``l2_spans``) is brought into L2 while the op runs (CUDA only)."""
     if not h.is_cuda:
         if delta is not None:
             h.copy_(h + delta)
@@ -39,13 +56,13 @@ def add_rms_norm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tens
     y = torch.empty_like(h)
     _native.check(_native.lib().dqg_add_rms_norm(
         h.data_ptr(), None if delta is None else delta.data_ptr(), weight.data_ptr(),
-        y.data_ptr(), m, hd, float(eps), _stream(h)))
+        y.data_ptr(), m, hd, float(eps), _spans_arg(prefetch), _stream(h)))
     return y
 
 
 def rope_kv_append(qkv: torch.Tensor, cos_row: torch.Tensor, sin_row: torch.Tensor,
                    k_cache: torch.Tensor, v_cache: torch.Tensor, pos: int, n_q_heads: int,
-                   n_kv_heads: int) -> torch.Tensor:
+                   n_kv_heads: int, prefetch=None) -> torch.Tensor:
     """Rotate the query and key heads of ``qkv`` [M, (Hq + 2 Hkv) D] at one
     position, write keys and values into slot ``pos`` of the caches
     [M, Hkv, capacity, D]; returns the rotated queries [M, Hq, D]."""
@@ -72,11 +89,11 @@ def rope_kv_append(qkv: torch.Tensor, cos_row: torch.Tensor, sin_row: torch.Tens
     _native.check(_native.lib().dqg_rope_kv_append(
         qkv.data_ptr(), cos_row.data_ptr(), sin_row.data_ptr(), q.data_ptr(),
         k_cache.data_ptr(), v_cache.data_ptr(), m, n_q_heads, n_kv_heads, d, pos,
-        k_cache.shape[2], _stream(qkv)))
+        k_cache.shape[2], _spans_arg(prefetch), _stream(qkv)))
     return q
 
 
-def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+def silu_mul(gate_up: torch.Tensor, prefetch=None) -> torch.Tensor:
     """SwiGLU of ``gate_up`` [M, 2 I] (gate, then up) -> fp16 [M, I]."""
     m, two_i = gate_up.shape
     i = two_i // 2
@@ -86,7 +103,7 @@ def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
         raise RuntimeError("silu_mul takes a contiguous float16 tensor")
     out = torch.empty((m, i), dtype=torch.float16, device=gate_up.device)
     _native.check(_native.lib().dqg_silu_mul(gate_up.data_ptr(), out.data_ptr(), m, i,
-                                             _stream(gate_up)))
+                                             _spans_arg(prefetch), _stream(gate_up)))
     return out
 
 

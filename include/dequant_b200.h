@@ -211,12 +211,30 @@ int dqg_stream_plan(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group
  */
 
 /*
+ * Byte ranges that a decode op brings into L2 while it runs, for the packed
+ * weights of a GEMV that follows it (every CTA of the op issues its share of
+ * bulk L2 prefetches before it waits for the previous kernel; the op's grid
+ * is widened to the SM count so that the prefetches are spread over every
+ * SM). A range whose start is not 16-byte aligned is trimmed to the aligned
+ * part; sizes are rounded down to 16 bytes. Up to 8 ranges, n of them used;
+ * NULL or n == 0 prefetches nothing. The ranges must be device memory of the
+ * current device that stays allocated while the op may run.
+ */
+typedef struct dqg_l2_spans {
+  const void *ptr[8];
+  uint64_t bytes[8];
+  int32_t n;
+} dqg_l2_spans;
+
+/*
  * Residual add + RMSNorm over rows of H values (H % 8 == 0, all pointers
  * 16-byte aligned): if delta != NULL, h[m] = fp16(h[m] + delta[m]) in place;
  * then y[m] = fp16((h[m] * rsqrt(mean(h[m]^2) + eps)) * weight), fp32 math.
+ * This op, dqg_rope_kv_append and dqg_silu_mul take an optional prefetch
+ * (dqg_l2_spans above).
  */
 int dqg_add_rms_norm(void *h, const void *delta, const void *weight, void *y, int64_t M,
-                     int64_t H, float eps, void *stream);
+                     int64_t H, float eps, const dqg_l2_spans *prefetch, void *stream);
 
 /*
  * Rotate-half RoPE at one position and KV-cache append. qkv is [M, (Hq +
@@ -228,7 +246,7 @@ int dqg_add_rms_norm(void *h, const void *delta, const void *weight, void *y, in
 int dqg_rope_kv_append(const void *qkv, const float *cos_row, const float *sin_row, void *q_out,
                        void *k_cache, void *v_cache, int64_t M, int64_t n_q_heads,
                        int64_t n_kv_heads, int64_t head_dim, int64_t pos, int64_t capacity,
-                       void *stream);
+                       const dqg_l2_spans *prefetch, void *stream);
 
 /*
  * Decode attention: one query token per sequence over its KV cache.
@@ -273,7 +291,8 @@ int dqg_decode_attention_noalloc(const void *q, const void *k_cache, const void 
  * SwiGLU: gate_up is [M, 2 I] (gate columns, then up columns);
  * out[m, i] = fp16(silu(gate) * up), silu(g) = g / (1 + exp(-g)) in fp32.
  */
-int dqg_silu_mul(const void *gate_up, void *out, int64_t M, int64_t I, void *stream);
+int dqg_silu_mul(const void *gate_up, void *out, int64_t M, int64_t I,
+                 const dqg_l2_spans *prefetch, void *stream);
 
 #ifdef __cplusplus
 }

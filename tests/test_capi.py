@@ -94,3 +94,14 @@ def test_weight_prefetch_switch_round_trips():
         assert lib.dqg_set_weight_prefetch(1) == 1
     finally:
         lib.dqg_set_weight_prefetch(prev)
+
+
+def test_l2_spans_layout_and_limits():
+    """dqg_l2_spans as ctypes lays out like the C struct (8 pointers, 8 sizes,
+    a count); at most 8 ranges, empty ranges dropped."""
+    s = _native.L2Spans.of([(0x1000, 4096), (0x9000, 0), (0x20000, 64)])
+    assert ctypes.sizeof(_native.L2Spans) == 8 * 8 + 8 * 8 + 8
+    assert s.n == 2 and s.ptr[1] == 0x20000 and s.bytes[0] == 4096
+    with pytest.raises(ValueError):
+        _native.L2Spans.of([(0x1000, 16)] * 9)
+    assert "dqg_l2_spans" in HEADER.read_text()

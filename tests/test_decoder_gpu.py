@@ -122,6 +122,57 @@ def test_graph_replay_matches_eager():
     assert torch.equal(out, eager)
 
 
+def test_l2_prefetch_changes_nothing_but_timing():
+    """The decoder with its element-wise ops prefetching later weights into
+    L2 gives bit-identical logits, eager and graph-replayed, to the one
+    without."""
+    q = QuantConfig(4, 128, False)
+    a = TPDecoder(SMALL, q, device="cuda", seed=7, batch=2, kv_len=64, l2_prefetch=True)
+    b = TPDecoder(SMALL, q, device="cuda", seed=7, batch=2, kv_len=64)
+    assert a._pf is not None and b._pf is None
+    plan = a.prefetch_plan()
+    assert plan[(0, "norm1")] == [(0, "qkv")] and plan[(1, "rope")] == [(1, "o"), (1, "gu")]
+    assert (1, "silu") not in plan           # nothing after the last layer's down projection
+    tokens = torch.tensor([17, 4001], device="cuda")
+    assert torch.equal(a.step(tokens, 64), b.step(tokens, 64))
+    gr = DecodeGraph(a, 64)
+    gr.tokens.copy_(tokens)
+    out = gr.replay().clone()
+    torch.cuda.synchronize()
+    gr.release()
+    assert torch.equal(out, b.step(tokens, 64))
+
+
+def test_prefetch_ranges_are_checked():
+    """Prefetch ranges go through the C ABI's checks: more than 8, a range
+    that runs past its device allocation and a host pointer are rejected; unaligned
+    starts and odd sizes are trimmed, and the op's output does not change."""
+    from dequant_project_b200 import _native
+    m, hd = 1, 1024
+    h = torch.randn(m, hd, device="cuda").half()
+    w = torch.ones(hd, device="cuda").half()
+    buf = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    ref = decode_ops.add_rms_norm(h, None, w, 1e-5)
+    ok = _native.L2Spans.of([(buf.data_ptr() + 3, 5000), (buf.data_ptr(), buf.numel())])
+    assert torch.equal(decode_ops.add_rms_norm(h, None, w, 1e-5, ok), ref)
+    assert torch.equal(decode_ops.silu_mul(torch.cat([h, h], 1), ok),
+                       decode_ops.silu_mul(torch.cat([h, h], 1)))
+    with pytest.raises(ValueError):
+        _native.L2Spans.of([(buf.data_ptr(), 16)] * 9)
+    # Past the end of the device allocation that holds buf (the caching
+    # allocator's segment, which may be larger than buf itself).
+    bad = _native.L2Spans.of([(buf.data_ptr(), 1 << 40)])
+    with pytest.raises(RuntimeError, match="past the end"):
+        decode_ops.add_rms_norm(h, None, w, 1e-5, bad)
+    host = torch.empty(4096, dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="prefetch range"):
+        decode_ops.add_rms_norm(h, None, w, 1e-5, _native.L2Spans.of([(host.data_ptr(), 4096)]))
+    over = _native.L2Spans.of([(buf.data_ptr(), 16)])
+    over.n = 9
+    with pytest.raises(RuntimeError, match="prefetch.n"):
+        decode_ops.add_rms_norm(h, None, w, 1e-5, over)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
