@@ -81,8 +81,7 @@ def lib() -> ctypes.CDLL:
     h.dqg_ipc_close.restype = i32
     h.dqg_ipc_close.argtypes = [vp]
     h.dqg_peer_allreduce.restype = i32
-    h.dqg_peer_allreduce.argtypes = [vp, vp, i64, u64p, u64p, vp, i64, i32, i32,
-                                     ctypes.c_uint64, vp]
+    h.dqg_peer_allreduce.argtypes = [vp, vp, i64, u64p, vp, i64, i32, i32, ctypes.c_uint64, vp]
     h.dqg_gemv_allreduce.restype = i32
     h.dqg_gemv_allreduce.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32,
                                      u64p, u64p, vp, i64, i32, i32, ctypes.c_uint64, vp]

@@ -756,9 +756,9 @@ int dqg_ipc_close(void* base) {
   return ok();
 }
 
-int dqg_peer_allreduce(const void* in, void* out, int64_t n, const uint64_t* peer_data,
-                       const uint64_t* peer_flags, uint32_t* ctl, int64_t cap, int rank,
-                       int world, uint64_t wait_ns, void* stream) {
+int dqg_peer_allreduce(const void* in, void* out, int64_t n, const uint64_t* peer_bufs,
+                       uint32_t* ctl, int64_t cap, int rank, int world, uint64_t wait_ns,
+                       void* stream) {
   if (world < 1 || world > dqg::kArMaxRanks || rank < 0 || rank >= world)
     return fail(DQG_ERR_INVALID, "rank %d / world %d out of range (at most %d ranks)", rank, world,
                 dqg::kArMaxRanks);
@@ -766,8 +766,7 @@ int dqg_peer_allreduce(const void* in, void* out, int64_t n, const uint64_t* pee
     return fail(DQG_ERR_INVALID, "n=%lld must be a positive multiple of 8 and at most cap=%lld",
                 (long long)n, (long long)cap);
   if (cap % 8 != 0) return fail(DQG_ERR_INVALID, "cap must be a multiple of 8");
-  if (in == nullptr || out == nullptr || peer_data == nullptr || peer_flags == nullptr ||
-      ctl == nullptr)
+  if (in == nullptr || out == nullptr || peer_bufs == nullptr || ctl == nullptr)
     return fail(DQG_ERR_INVALID, "pointers must not be null");
   if (reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return fail(DQG_ERR_INVALID, "in and out must be 16-byte aligned");
@@ -779,10 +778,9 @@ int dqg_peer_allreduce(const void* in, void* out, int64_t n, const uint64_t* pee
   p.n = n;
   p.cap = cap;
   for (int r = 0; r < world; ++r) {
-    if (peer_data[r] == 0 || peer_flags[r] == 0 || peer_data[r] % 16)
+    if (peer_bufs[r] == 0 || peer_bufs[r] % 16)
       return fail(DQG_ERR_INVALID, "peer buffers of rank %d missing or misaligned", r);
-    p.peer_data[r] = peer_data[r];
-    p.peer_flags[r] = peer_flags[r];
+    p.peer_data[r] = peer_bufs[r];
   }
   p.ctl = ctl;
   p.rank = rank;

@@ -139,8 +139,9 @@ struct PeerReduceParams {
   __half* out;
   long long n;                    // elements, a multiple of 8
   long long cap;                  // elements per parity half of each exchange buffer
-  unsigned long long peer_data[kArMaxRanks];   // each rank's exchange buffer (2 * cap fp16)
-  unsigned long long peer_flags[kArMaxRanks];  // each rank's flags [chunks][world] u32
+  // Each rank's receive buffer: [parity 2][source rank world][cap / 2]
+  // 8-byte packets (32-bit data word, 32-bit epoch flag).
+  unsigned long long peer_data[kArMaxRanks];
   uint32_t* ctl;                  // this rank's [epoch, ticket]
   int rank, world;
   unsigned long long wait_ns;

@@ -1,30 +1,29 @@
 // One-shot all-reduce of small fp16 tensors over NVLink peer memory, for the
 // row-parallel layers of the tensor-parallel decoder (two per layer, 8-128 KB
 // each). The reference has no collective; it only models the decoder's bytes
-// (dequant/byte_model.py:179-251). NCCL's ring/tree algorithms pay several
-// link round trips per call; at these sizes the call is latency-bound, so a
-// single exchange round is cheaper:
+// (dequant/byte_model.py:179-251). At these sizes a collective is bound by
+// latency, not bandwidth, so the exchange takes one one-way trip over NVLink:
 //
-//   1. every rank copies its input chunk into its own exchange buffer;
-//   2. it raises a flag in every peer's flag array (plain stores through an
-//      IPC mapping of the peer's memory, ordered by a system-scope fence);
-//   3. it waits until every peer's flag for the chunk has arrived in its own
-//      flag array (bounded: a wait that runs out sets the device status bit
-//      and the kernel returns);
-//   4. it reads the chunk from every rank's buffer (plain loads from peer
-//      memory, no bulk copies, no multicast) and sums in rank order in fp32,
-//      rounding once to fp16, so every rank gets bit-identical results.
+//   1. every rank stores its input into every peer's receive buffer as 8-byte
+//      packets (one 32-bit data word and one 32-bit flag holding this call's
+//      epoch), plain stores through IPC mappings of the peers' memory;
+//   2. it polls its own receive buffer (local memory) until every peer's
+//      packets carry this call's epoch (bounded: a wait that runs out sets
+//      the device status bit and those outputs stay unwritten);
+//   3. it sums the ranks' words in rank order in fp32 and rounds once to
+//      fp16, so every rank gets bit-identical results.
 //
-// Exchange buffers are double-buffered by the parity of a per-rank call
+// A packet's data and flag travel in one aligned 8-byte store (two packets
+// per 16-byte store), so a reader that sees the flag sees the data: no
+// fences, no separate flag round trip and no loads from peer memory.
+//
+// Receive buffers are double-buffered by the parity of a per-rank call
 // counter ("epoch") that lives in device memory and is advanced by the last
 // CTA of each call, so the kernel can be captured in a CUDA graph (nothing
-// per call comes from the host). Flags hold the epoch of the last call that
-// raised them and only grow, so a wait accepts any value >= its epoch.
-//
-// Buffer reuse: call e writes buffer e & 1, which call e + 2 overwrites. A
-// rank starts call e + 2 only after its call e + 1 saw every peer's call e + 1
-// flag, which a peer raises only after it finished call e (its reads of our
-// buffer e & 1 included).
+// per call comes from the host). Call e writes parity e & 1 of every peer's
+// buffer, which call e + 2 overwrites. A rank starts call e + 2 only after its
+// call e + 1 received every peer's call e + 1 packets, which a peer sends only
+// after it finished reading its call e packets.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -38,76 +37,88 @@ namespace {
 
 constexpr int kArThreads = 256;
 
-__device__ __forceinline__ void fence_sys() { fence_acq_rel_sys(); }
+__device__ __forceinline__ void st_volatile_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
+                                               uint32_t d) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
 
-// 16 bytes from a (possibly peer) address, bypassing L1: the data were written
-// by another GPU during this call.
-__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+// 16 bytes of this GPU's memory that a peer is writing during the call
+// (volatile: never served from a stale L1 line).
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
   uint4 v;
-  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p)
                : "memory");
   return v;
 }
 
+// Each thread owns two consecutive 32-bit words of the input (four fp16
+// values): one 16-byte pair of packets per source rank.
 __global__ void __launch_bounds__(kArThreads)
     peer_allreduce_kernel(const __grid_constant__ PeerReduceParams p) {
   pdl_wait_prior_grid();
   if (threadIdx.x == 0) pdl_launch_dependents();
-  const int chunk = blockIdx.x;
-  const int tid = threadIdx.x;
   const uint32_t ep = *reinterpret_cast<volatile const uint32_t*>(p.ctl) + 1u;
-  const int64_t par_off = static_cast<int64_t>(ep & 1u) * p.cap;  // elements
-  const int64_t e0 = static_cast<int64_t>(chunk) * kArChunk;
-  const int64_t left = p.n - e0;
-  const int n_here = static_cast<int>(left < kArChunk ? left : kArChunk);
-  __half* mine = reinterpret_cast<__half*>(p.peer_data[p.rank]) + par_off + e0;
-
-  // 1. This rank's chunk into its exchange buffer (n is a multiple of 8).
-  for (int v = tid; v < n_here / 8; v += kArThreads)
-    reinterpret_cast<uint4*>(mine)[v] = reinterpret_cast<const uint4*>(p.in + e0)[v];
-  __syncthreads();
-  // 2. Raise this chunk's flag in every rank's flag array (ours included).
-  if (tid < p.world) {
-    fence_sys();
-    uint32_t* flags = reinterpret_cast<uint32_t*>(p.peer_flags[tid]);
-    st_relaxed_sys(flags + chunk * p.world + p.rank, ep);
-  }
-  // 3. Wait for every rank's flag of this chunk in our own array.
-  bool ok = true;
-  if (tid < p.world) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(p.peer_flags[p.rank]) +
-                        chunk * p.world + tid;
-    ok = wait_flag_sys(f, ep, p.wait_ns);
-    fence_sys();
-  }
-  ok = __syncthreads_and(ok);
-  // 4. Sum the chunk over ranks in rank order, fp32, one rounding.
-  if (ok) {
-    for (int v = tid; v < n_here / 8; v += kArThreads) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int r = 0; r < p.world; ++r) {
-        const __half* src = reinterpret_cast<const __half*>(p.peer_data[r]) + par_off + e0;
-        const uint4 w = ld_cg_v4(reinterpret_cast<const uint4*>(src) + v);
-        const __half2* h2 = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
-          acc[2 * i] += f.x;
-          acc[2 * i + 1] += f.y;
+  const int64_t slot = p.cap / 2;  // packets per (parity, source rank)
+  const int64_t pair = static_cast<int64_t>(blockIdx.x) * kArThreads + threadIdx.x;
+  const bool mine = pair * 4 < p.n;
+  const int64_t base = static_cast<int64_t>(ep & 1u) * p.world * slot;  // packets
+  if (mine) {
+    const uint2 d = reinterpret_cast<const uint2*>(p.in)[pair];
+    // 1. This rank's words into slot `rank` of every peer's receive buffer.
+    for (int r = 0; r < p.world; ++r) {
+      if (r == p.rank) continue;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.peer_data[r]) +
+                     (base + static_cast<int64_t>(p.rank) * slot + pair * 2) * 8;
+      st_volatile_v4(dst, d.x, ep, d.y, ep);
+    }
+    // 2. + 3. Every peer's packets from this rank's own buffer, summed with
+    // this rank's words in rank order.
+    const uint8_t* own = reinterpret_cast<const uint8_t*>(p.peer_data[p.rank]);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    uint64_t t0 = 0;
+    for (int r = 0; r < p.world && ok; ++r) {
+      uint32_t w0 = d.x, w1 = d.y;
+      if (r != p.rank) {
+        const uint8_t* src = own + (base + static_cast<int64_t>(r) * slot + pair * 2) * 8;
+        uint4 v = ld_volatile_v4(src);
+        for (uint32_t spin = 1; v.y != ep || v.w != ep; ++spin) {
+          if ((spin & 63u) == 0u) {
+            const uint64_t now = globaltimer();
+            if (t0 == 0) {
+              t0 = now;
+            } else if (now - t0 > p.wait_ns) {
+              atomicOr(&g_status, kStatusWaitTimeout);
+              ok = false;
+              break;
+            }
+          }
+          v = ld_volatile_v4(src);
         }
+        w0 = v.x;
+        w1 = v.z;
       }
-      uint4 o;
-      __half2* oh = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
-      reinterpret_cast<uint4*>(p.out + e0)[v] = o;
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w0));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w1));
+      acc[0] += a.x;
+      acc[1] += a.y;
+      acc[2] += b.x;
+      acc[3] += b.y;
+    }
+    if (ok) {
+      const __half2 o0 = __floats2half2_rn(acc[0], acc[1]);
+      const __half2 o1 = __floats2half2_rn(acc[2], acc[3]);
+      reinterpret_cast<uint2*>(p.out)[pair] = make_uint2(
+          *reinterpret_cast<const uint32_t*>(&o0), *reinterpret_cast<const uint32_t*>(&o1));
     }
   }
-  // 5. The last CTA of the call advances the epoch for the next call.
+  // The last CTA of the call advances the epoch for the next call.
   __syncthreads();
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t t = atomicAdd(p.ctl + 1, 1u);
     if (t == gridDim.x - 1) {
@@ -121,9 +132,9 @@ __global__ void __launch_bounds__(kArThreads)
 }  // namespace
 
 cudaError_t launch_peer_allreduce(const PeerReduceParams& p, cudaStream_t stream) {
-  const int chunks = static_cast<int>((p.n + kArChunk - 1) / kArChunk);
+  const int64_t pairs = p.n / 4;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(chunks);
+  cfg.gridDim = dim3(static_cast<unsigned>((pairs + kArThreads - 1) / kArThreads));
   cfg.blockDim = dim3(kArThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

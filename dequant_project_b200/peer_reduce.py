@@ -7,13 +7,14 @@ the reference itself has no multi-GPU code). At these
 sizes a collective is bound by latency, not bandwidth, so this replaces NCCL's
 algorithms with one exchange round through memory every rank can address:
 
-* at set-up, each rank allocates one exchange buffer (two parity halves of
-  ``cap`` fp16 values plus a flag array) and a two-word call counter, zeroed;
-  the buffers' CUDA IPC handles are swapped over the process group
+* at set-up, each rank allocates one buffer (the all-reduce's receive
+  packets, the fused GEMV's fp32 exchange and its flags) and call counters,
+  zeroed; the buffers' CUDA IPC handles are swapped over the process group
   (``all_gather_object``) and every peer's buffer is mapped into this process;
-* each call (``dqg_peer_allreduce`` in libdequant_b200.so) copies the input
-  into this rank's buffer, raises a flag in every peer's flag array, waits
-  (bounded) for every peer's flag and sums all ranks' buffers in rank order in
+* each call (``dqg_peer_allreduce`` in libdequant_b200.so) stores the input
+  into every peer's receive buffer as packets that carry the call's epoch
+  beside each data word, waits (bounded) until every peer's packets have
+  arrived in this rank's buffer and sums all ranks' values in rank order in
   fp32 with one rounding, so every rank gets the same bits;
 * ``gemv`` runs a row-parallel layer as ONE kernel (``dqg_gemv_allreduce``):
   the GEMV's CTAs write their rows' fp32 partials into this buffer and
@@ -34,7 +35,6 @@ import torch
 
 from dequant_project_b200 import _native
 
-CHUNK = 2048          # elements per CTA of the kernel (one flag per chunk and rank)
 MAX_RANKS = 8
 MAX_GEMV_CTAS = 1024  # flags of the fused row-parallel GEMV: one per CTA and rank
 HANDLE_BYTES = 64     # sizeof(cudaIpcMemHandle_t)
@@ -81,21 +81,21 @@ class PeerAllReduce:
             raise ValueError("max_elems must be at least 8")
         self.device = torch.device(device)
         self.cap = _round_up(max_elems, 8)
-        self.chunks = (self.cap + CHUNK - 1) // CHUNK
         self.wait_ns = int(wait_ns)
         self._ipc = ipc if ipc is not None else CudaIpc()
-        # One allocation, so one handle per rank: [exchange data (fp32, two
-        # parity halves of cap values; the fp16 all-reduce uses its front) |
-        # all-reduce flags | fused-GEMV flags].
+        # One allocation, so one handle per rank: [all-reduce receive packets
+        # (two parity halves of `world` slots of cap / 2 eight-byte packets) |
+        # fused-GEMV exchange (fp32, two parity halves of cap values) |
+        # fused-GEMV flags].
+        packet_bytes = 8 * self.world * self.cap
         data_bytes = 2 * self.cap * 4
-        ar_flag_bytes = self.chunks * self.world * 4
         gemv_flag_bytes = MAX_GEMV_CTAS * self.world * 4
-        self.buffer = torch.zeros(data_bytes + ar_flag_bytes + gemv_flag_bytes,
+        self.buffer = torch.zeros(packet_bytes + data_bytes + gemv_flag_bytes,
                                   dtype=torch.uint8, device=self.device)
         # Call counters: [all-reduce epoch, ticket, fused-GEMV epoch, ticket].
         self.ctl = torch.zeros(4, dtype=torch.int32, device=self.device)
-        self._flag_off = data_bytes
-        self._gemv_flag_off = data_bytes + ar_flag_bytes
+        self._data_off = packet_bytes
+        self._gemv_flag_off = packet_bytes + data_bytes
         handle, offset = self._ipc.export(self.buffer.data_ptr())
         infos = [None] * self.world
         dist.all_gather_object(infos, (self.rank, handle, offset), group=group)
@@ -110,11 +110,11 @@ class PeerAllReduce:
                 base = self._ipc.open(h)
                 self._opened.append(base)
                 data_ptrs.append(base + off)
-        self.peer_data = (ctypes.c_uint64 * self.world)(*data_ptrs)
-        self.peer_flags = (ctypes.c_uint64 * self.world)(*[p + self._flag_off for p in data_ptrs])
+        self.peer_bufs = (ctypes.c_uint64 * self.world)(*data_ptrs)
+        self.peer_data = (ctypes.c_uint64 * self.world)(*[p + self._data_off for p in data_ptrs])
         self.peer_gemv_flags = (ctypes.c_uint64 * self.world)(
             *[p + self._gemv_flag_off for p in data_ptrs])
-        # No rank may raise a flag in a buffer its peer has not mapped yet.
+        # No rank may write into a buffer its peer has not mapped yet.
         dist.barrier(group=group)
 
     def __call__(self, t: torch.Tensor) -> torch.Tensor:
@@ -127,7 +127,7 @@ class PeerAllReduce:
         if n % 8 or n > self.cap or n == 0:
             raise RuntimeError(f"{n} values: need a positive multiple of 8 up to {self.cap}")
         _native.check(_native.lib().dqg_peer_allreduce(
-            t.data_ptr(), t.data_ptr(), n, self.peer_data, self.peer_flags, self.ctl.data_ptr(),
+            t.data_ptr(), t.data_ptr(), n, self.peer_bufs, self.ctl.data_ptr(),
             self.cap, self.rank, self.world, self.wait_ns,
             torch.cuda.current_stream(self.device).cuda_stream))
         return t

@@ -148,22 +148,24 @@ int dqg_ipc_close(void *base);
  * allowed), summed in rank order in fp32 and rounded once, so every rank gets
  * the same bits. Replaces the NCCL all-reduce that follows each row-parallel
  * layer of the decoder step (the reference has none; it models the bytes in
- * dequant/byte_model.py:179-251).
- *   peer_data[r]  : rank r's exchange buffer, 2 * cap fp16, 16-byte aligned
- *                   (this rank's own buffer at r == rank, IPC mappings of the
- *                   others), zero-initialised once;
- *   peer_flags[r] : rank r's flag array, ceil(cap / 2048) * world uint32,
- *                   zero-initialised once;
- *   ctl           : this rank's two uint32 call counters, zero-initialised once.
+ * dequant/byte_model.py:179-251). Each rank stores its values straight into
+ * every peer's receive buffer as 8-byte packets (a 32-bit data word and a
+ * 32-bit flag carrying the call's epoch, written together) and polls its own
+ * buffer until every peer's packets of the call have arrived.
+ *   peer_bufs[r] : rank r's receive buffer of 8 * world * cap bytes (two
+ *                  parity halves of `world` slots of cap / 2 packets),
+ *                  16-byte aligned (this rank's own buffer at r == rank, IPC
+ *                  mappings of the others), zero-initialised once;
+ *   ctl          : this rank's two uint32 call counters, zero-initialised once.
  * Every rank must make the same sequence of calls. Each wait for a peer is
  * bounded by wait_ns (0 = 2 s); a wait that runs out sets bit 0 of
- * dqg_device_status and leaves out unwritten. Peer memory is read with plain
- * loads only (no bulk copies, no multicast). Host arrays peer_data and
- * peer_flags are read during the call only; nothing is allocated.
+ * dqg_device_status and leaves those values of out unwritten. Peer memory is
+ * only written, with plain stores (no loads, bulk copies or multicast). The
+ * host array peer_bufs is read during the call only; nothing is allocated.
  */
-int dqg_peer_allreduce(const void *in, void *out, int64_t n, const uint64_t *peer_data,
-                       const uint64_t *peer_flags, uint32_t *ctl, int64_t cap, int rank,
-                       int world, uint64_t wait_ns, void *stream);
+int dqg_peer_allreduce(const void *in, void *out, int64_t n, const uint64_t *peer_bufs,
+                       uint32_t *ctl, int64_t cap, int rank, int world, uint64_t wait_ns,
+                       void *stream);
 
 /*
  * Row-parallel GEMV fused with its all-reduce: every rank passes its slice of

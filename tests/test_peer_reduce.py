@@ -1,8 +1,9 @@
 """Host side of the peer all-reduce, on gloo CPU ranks (no GPU): every rank
 maps every other rank's exchange buffer exactly once, builds its pointer
 tables in rank order (its own buffer in its own slot, peers at their handle's
-offset), sizes the buffer for both parity halves and one flag per chunk and
-rank, releases each mapping once, and refuses calls after close()."""
+offset), lays the buffer out as the all-reduce's receive packets (both
+parity halves, one slot per rank), the fused GEMV's exchange and its flags,
+releases each mapping once, and refuses calls after close()."""
 
 from __future__ import annotations
 
@@ -49,13 +50,13 @@ def test_gloo_ranks_exchange_and_map_every_peer(world):
         assert opened_ranks == others                     # each peer once, in rank order
         for s in others:                                  # the handle a peer exported
             assert f"rank{s}:{out[s][1]['own']}" in info["opened"]
-        assert info["data"][r] == info["own"]
-        assert len(info["data"]) == world and len(set(info["data"])) == world
-        flag_off = 2 * info["cap"] * 4                    # fp32 exchange data first
-        assert [f - d for f, d in zip(info["flags"], info["data"])] == [flag_off] * world
-        gemv_off = flag_off + info["chunks"] * world * 4
-        assert [f - d for f, d in zip(info["gemv_flags"], info["data"])] == [gemv_off] * world
-        assert info["cap"] == 5000 and info["chunks"] == 3
+        assert info["bufs"][r] == info["own"]
+        assert len(info["bufs"]) == world and len(set(info["bufs"])) == world
+        packet_bytes = 8 * world * info["cap"]            # all-reduce receive packets first
+        assert [d - b for d, b in zip(info["data"], info["bufs"])] == [packet_bytes] * world
+        gemv_off = packet_bytes + 2 * info["cap"] * 4     # then the fused GEMV's fp32 exchange
+        assert [f - b for f, b in zip(info["gemv_flags"], info["bufs"])] == [gemv_off] * world
+        assert info["cap"] == 5000
         assert info["nbytes"] == gemv_off + 1024 * world * 4
         assert info["closed"] == world - 1                # close() is idempotent
         assert "after close" in info["after_close"]

@@ -1,9 +1,9 @@
 """The one-shot peer all-reduce kernel on the GPU.
 
 On one GPU, one launch at a time: the exchange protocol is exercised with a
-second rank's buffer that lives on the same device and whose flags the test
-raises (or leaves down) before the launch, so no kernel ever waits for another
-kernel. With two GPUs: two NCCL processes, the kernel against the fp32 sum of
+second rank's buffer that lives on the same device, and the packets that rank
+would have sent are written (or left out) by the test before the launch, so
+no kernel ever waits for another kernel. With two GPUs: two NCCL processes, the kernel against the fp32 sum of
 both ranks' inputs (bit-exact), eager and replayed from a CUDA graph, and the
 decoder with the peer all-reduce against the decoder with NCCL's.
 """
@@ -19,74 +19,77 @@ import torch
 import torch.multiprocessing as mp
 
 from dequant_project_b200 import _native
-from dequant_project_b200.peer_reduce import CHUNK
 
 pytestmark = pytest.mark.gpu
 
 
 def _buffers(cap, world, dev):
-    chunks = (cap + CHUNK - 1) // CHUNK
-    data_bytes = 2 * cap * 2
-    return torch.zeros(data_bytes + chunks * world * 4, dtype=torch.uint8, device=dev), data_bytes
+    """A receive buffer: [parity 2][source rank world][cap / 2] packets of
+    (int32 data word, int32 epoch)."""
+    return torch.zeros(8 * world * cap, dtype=torch.uint8, device=dev)
 
 
-def _call(inp, out, n, bufs, flag_off, ctl, cap, rank, world, wait_ns=0):
+def _packets(buf, cap, world):
+    return buf.view(torch.int32).view(2, world, cap // 2, 2)
+
+
+def _call(inp, out, n, bufs, ctl, cap, rank, world, wait_ns=0):
     ptrs = (ctypes.c_uint64 * world)(*[b.data_ptr() for b in bufs])
-    flags = (ctypes.c_uint64 * world)(*[b.data_ptr() + flag_off for b in bufs])
     return _native.lib().dqg_peer_allreduce(
-        inp.data_ptr(), out.data_ptr(), n, ptrs, flags, ctl.data_ptr(), cap, rank, world, wait_ns,
+        inp.data_ptr(), out.data_ptr(), n, ptrs, ctl.data_ptr(), cap, rank, world, wait_ns,
         torch.cuda.current_stream().cuda_stream)
 
 
-@pytest.mark.parametrize("n", [8, 4096, 2 * CHUNK + 24, 65536])
-def test_sums_a_peer_whose_flags_are_up(cuda_device, n):
+@pytest.mark.parametrize("n", [8, 4096, 4104, 65536])
+def test_sums_a_peer_whose_packets_have_arrived(cuda_device, n):
     cap, world = 65536, 2
-    mine, off = _buffers(cap, world, cuda_device)
-    peer, _ = _buffers(cap, world, cuda_device)
+    mine, peer = _buffers(cap, world, cuda_device), _buffers(cap, world, cuda_device)
     ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
     g = torch.Generator(device=cuda_device).manual_seed(n)
     a = torch.randn(n, generator=g, device=cuda_device).half()
     b = torch.randn(n, generator=g, device=cuda_device).half()
-    # The first call has epoch 1 and reads parity half 1 of every buffer.
-    peer[:off].view(torch.float16)[cap:cap + n] = b
-    chunks = (n + CHUNK - 1) // CHUNK
-    my_flags = mine[off:].view(torch.int32)
-    my_flags[torch.arange(chunks, device=cuda_device) * world + 1] = 7   # rank 1 is ahead
+    # The first call has epoch 1: rank 1's packets sit in parity half 1, slot 1
+    # of this rank's buffer (as rank 1's stores would have left them).
+    pk = _packets(mine, cap, world)
+    pk[1, 1, :n // 2, 0] = b.view(torch.int32)
+    pk[1, 1, :n // 2, 1] = 1
     out = torch.empty_like(a)
     _native.device_status(cuda_device.index, reset=True)
-    _native.check(_call(a, out, n, [mine, peer], off, ctl, cap, 0, world))
+    _native.check(_call(a, out, n, [mine, peer], ctl, cap, 0, world))
     torch.cuda.synchronize()
     assert torch.equal(out, (a.float() + b.float()).half())
-    # This rank's chunk sits in its own buffer; its flag went up in both arrays.
-    assert torch.equal(mine[:off].view(torch.float16)[cap:cap + n], a)
-    idx = torch.arange(chunks, device=cuda_device) * world
-    assert bool((my_flags[idx] == 1).all())
-    assert bool((peer[off:].view(torch.int32)[idx] == 1).all())
+    # This rank's words went to slot 0 of the peer's buffer, flagged with the epoch.
+    pp = _packets(peer, cap, world)
+    assert torch.equal(pp[1, 0, :n // 2, 0], a.view(torch.int32))
+    assert bool((pp[1, 0, :n // 2, 1] == 1).all())
+    assert int(pp[0].abs().sum()) == 0 and int(pp[1, 1].abs().sum()) == 0
     assert ctl.tolist() == [1, 0]                 # next call: epoch 2, parity 0
     assert _native.device_status(cuda_device.index) == 0
 
 
 def test_single_rank_is_a_copy(cuda_device):
     cap = 4096
-    mine, off = _buffers(cap, 1, cuda_device)
+    mine = _buffers(cap, 1, cuda_device)
     ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
     a = torch.randn(cap, device=cuda_device).half()
     out = torch.empty_like(a)
     for _ in range(3):                            # epochs 1, 2, 3: both parity halves
-        _native.check(_call(a, out, cap, [mine], off, ctl, cap, 0, 1))
+        _native.check(_call(a, out, cap, [mine], ctl, cap, 0, 1))
     torch.cuda.synchronize()
     assert torch.equal(out, a) and ctl.tolist() == [3, 0]
 
 
-def test_missing_peer_flag_gives_up_and_reports(cuda_device):
+def test_missing_peer_gives_up_and_reports(cuda_device):
     cap, world, n = 8192, 2, 8192
-    mine, off = _buffers(cap, world, cuda_device)
-    peer, _ = _buffers(cap, world, cuda_device)
+    mine, peer = _buffers(cap, world, cuda_device), _buffers(cap, world, cuda_device)
+    # Packets of an older call (epoch 3) must not be taken for this one's.
+    pk = _packets(mine, cap, world)
+    pk[1, 1, :, 1] = 3
     ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
     a = torch.randn(n, device=cuda_device).half()
     out = torch.full_like(a, 3.0)
     _native.device_status(cuda_device.index, reset=True)
-    _native.check(_call(a, out, n, [mine, peer], off, ctl, cap, 0, world, wait_ns=20_000_000))
+    _native.check(_call(a, out, n, [mine, peer], ctl, cap, 0, world, wait_ns=20_000_000))
     torch.cuda.synchronize()                      # returns: the wait ran out after 20 ms
     assert _native.device_status(cuda_device.index, reset=True) & 1
     assert bool((out == 3.0).all()), "a call whose peer never arrived wrote its output"
@@ -96,14 +99,14 @@ def test_missing_peer_flag_gives_up_and_reports(cuda_device):
 
 def test_rejects_bad_arguments(cuda_device):
     cap = 4096
-    mine, off = _buffers(cap, 2, cuda_device)
+    mine = _buffers(cap, 2, cuda_device)
     ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
     a = torch.zeros(cap, dtype=torch.float16, device=cuda_device)
     for kw, msg in ((dict(n=12), b"multiple of 8"), (dict(n=cap + 8), b"at most cap"),
                     (dict(rank=2), b"out of range"), (dict(wait_ns=5), b"wait_ns")):
         args = dict(n=cap, rank=0, world=2, wait_ns=0)
         args.update(kw)
-        rc = _call(a, a, args["n"], [mine, mine], off, ctl, cap, args["rank"], args["world"],
+        rc = _call(a, a, args["n"], [mine, mine], ctl, cap, args["rank"], args["world"],
                    args["wait_ns"])
         assert rc == 1 and msg in _native.lib().dqg_last_error()
 

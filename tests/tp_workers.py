@@ -273,10 +273,9 @@ def peer_exchange(rank, world, port, queue):
         dist = _init(rank, world, port, "gloo", 60)
         ipc = FakeIpc(rank)
         ar = PeerAllReduce(None, torch.device("cpu"), 5000, ipc=ipc)
-        info = {"opened": list(ipc.opened), "data": list(ar.peer_data),
-                "flags": list(ar.peer_flags), "gemv_flags": list(ar.peer_gemv_flags),
-                "own": ar.buffer.data_ptr(), "cap": ar.cap,
-                "chunks": ar.chunks, "nbytes": ar.buffer.numel()}
+        info = {"opened": list(ipc.opened), "bufs": list(ar.peer_bufs),
+                "data": list(ar.peer_data), "gemv_flags": list(ar.peer_gemv_flags),
+                "own": ar.buffer.data_ptr(), "cap": ar.cap, "nbytes": ar.buffer.numel()}
         ar.close()
         ar.close()
         info["closed"] = len(ipc.closed)
