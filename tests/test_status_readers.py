@@ -10,7 +10,10 @@ import re
 from conftest import ROOT
 
 CSRC = ROOT / "dequant_project_b200" / "csrc"
-WAITS = re.compile(r"\b(warp_wait|mbar_wait|warp_wait_cluster|wait_flag_sys)\s*\(")
+# A bounded wait through the shared helpers, or a kernel's own poll that sets
+# the timeout bit itself.
+WAITS = re.compile(r"\b(warp_wait|mbar_wait|warp_wait_cluster|wait_flag_sys)\s*\(|"
+                   r"atomicOr\(&g_status, kStatusWaitTimeout\)")
 
 
 def _text_with_includes(path):
