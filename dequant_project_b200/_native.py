@@ -82,6 +82,9 @@ def lib() -> ctypes.CDLL:
     h.dqg_ipc_close.argtypes = [vp]
     h.dqg_peer_allreduce.restype = i32
     h.dqg_peer_allreduce.argtypes = [vp, vp, i64, u64p, vp, i64, i32, i32, ctypes.c_uint64, vp]
+    h.dqg_peer_allreduce_add_rms_norm.restype = i32
+    h.dqg_peer_allreduce_add_rms_norm.argtypes = [vp, vp, vp, vp, i64, i64, ctypes.c_float, u64p,
+                                                  vp, i64, i32, i32, ctypes.c_uint64, vp]
     h.dqg_gemv_allreduce.restype = i32
     h.dqg_gemv_allreduce.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32,
                                      u64p, u64p, vp, i64, i32, i32, ctypes.c_uint64, vp]
@@ -104,7 +107,8 @@ EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_deq
             "dqg_stream_plan", "dqg_set_weight_prefetch", "dqg_debug_gemv_starved",
             "dqg_set_gemv_path", "dqg_decode_attention_workspace", "dqg_decode_attention",
             "dqg_gemv_allreduce", "dqg_decode_attention_noalloc",
-            "dqg_ipc_export", "dqg_ipc_open", "dqg_ipc_close", "dqg_peer_allreduce")
+            "dqg_ipc_export", "dqg_ipc_open", "dqg_ipc_close", "dqg_peer_allreduce",
+            "dqg_peer_allreduce_add_rms_norm")
 
 
 def check(rc: int) -> None:

@@ -791,6 +791,55 @@ int dqg_peer_allreduce(const void* in, void* out, int64_t n, const uint64_t* pee
   return ok();
 }
 
+int dqg_peer_allreduce_add_rms_norm(const void* partial, void* h, const void* weight, void* y,
+                                    int64_t M, int64_t H, float eps, const uint64_t* peer_bufs,
+                                    uint32_t* ctl, int64_t cap, int rank, int world,
+                                    uint64_t wait_ns, void* stream) {
+  if (world < 1 || world > dqg::kArMaxRanks || rank < 0 || rank >= world)
+    return fail(DQG_ERR_INVALID, "rank %d / world %d out of range (at most %d ranks)", rank, world,
+                dqg::kArMaxRanks);
+  if (H < 8 || H % 8 != 0 || H > dqg::kArNormMaxH)
+    return fail(DQG_ERR_INVALID, "H must be a multiple of 8 in [8, %d], got %lld", dqg::kArNormMaxH,
+                (long long)H);
+  if (M < 1 || M > 65535 || M * H > cap)
+    return fail(DQG_ERR_INVALID, "M=%lld rows of H=%lld must be at least one and fit cap=%lld",
+                (long long)M, (long long)H, (long long)cap);
+  if (cap % 8 != 0) return fail(DQG_ERR_INVALID, "cap must be a multiple of 8");
+  if (!(eps >= 0.f)) return fail(DQG_ERR_INVALID, "eps must be non-negative");
+  if (partial == nullptr || h == nullptr || weight == nullptr || y == nullptr ||
+      peer_bufs == nullptr || ctl == nullptr)
+    return fail(DQG_ERR_INVALID, "pointers must not be null");
+  const void* al[4] = {partial, h, weight, y};
+  for (const void* q : al)
+    if (reinterpret_cast<uintptr_t>(q) % 16)
+      return fail(DQG_ERR_INVALID, "partial, h, weight and y must be 16-byte aligned");
+  if (wait_ns != 0 && (wait_ns < 1000000ull || wait_ns > 10000000000ull))
+    return fail(DQG_ERR_INVALID, "wait_ns must be 0 (default) or in [1 ms, 10 s]");
+  dqg::PeerNormParams q = {};
+  q.ar.in = static_cast<const __half*>(partial);
+  q.ar.out = nullptr;
+  q.ar.n = M * H;
+  q.ar.cap = cap;
+  for (int r = 0; r < world; ++r) {
+    if (peer_bufs[r] == 0 || peer_bufs[r] % 16)
+      return fail(DQG_ERR_INVALID, "peer buffers of rank %d missing or misaligned", r);
+    q.ar.peer_data[r] = peer_bufs[r];
+  }
+  q.ar.ctl = ctl;
+  q.ar.rank = rank;
+  q.ar.world = world;
+  q.ar.wait_ns = wait_ns ? wait_ns : 2000000000ull;
+  q.h = static_cast<__half*>(h);
+  q.w = static_cast<const __half*>(weight);
+  q.y = static_cast<__half*>(y);
+  q.M = static_cast<int>(M);
+  q.H = static_cast<int>(H);
+  q.eps = eps;
+  cudaError_t e = dqg::launch_peer_allreduce_add_rms_norm(q, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "peer_allreduce_add_rms_norm launch");
+  return ok();
+}
+
 int dqg_device_status(int device, uint32_t* status, int reset) {
   if (status == nullptr) return fail(DQG_ERR_INVALID, "status must not be null");
   cudaError_t e = dqg::read_device_status(device, status, reset != 0);

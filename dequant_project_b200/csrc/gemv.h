@@ -131,14 +131,14 @@ bool plan_stream(int M, int N, int K, int bits, int group_size, int num_sms, Str
 
 // ------------------------------------------------------- peer all-reduce
 // One-shot all-reduce of fp16 tensors over peer memory (peer_reduce.cu).
-constexpr int kArChunk = 2048;    // elements per CTA (one flag per chunk and rank)
 constexpr int kArMaxRanks = 8;
+constexpr int kArNormMaxH = 8192;  // row length of the fused all-reduce + RMSNorm
 
 struct PeerReduceParams {
   const __half* in;
   __half* out;
   long long n;                    // elements, a multiple of 8
-  long long cap;                  // elements per parity half of each exchange buffer
+  long long cap;                  // elements of one parity half (packets per slot: cap / 2)
   // Each rank's receive buffer: [parity 2][source rank world][cap / 2]
   // 8-byte packets (32-bit data word, 32-bit epoch flag).
   unsigned long long peer_data[kArMaxRanks];
@@ -148,6 +148,19 @@ struct PeerReduceParams {
 };
 
 cudaError_t launch_peer_allreduce(const PeerReduceParams& p, cudaStream_t stream);
+
+// The all-reduce of a row-parallel layer's partial rows fused with the
+// residual add + RMSNorm that follows it: in = this rank's partial [M, H]
+// (n = M * H), h [M, H] updated in place, y = RMSNorm(h) * w.
+struct PeerNormParams {
+  PeerReduceParams ar;
+  __half* h;
+  const __half* w;
+  __half* y;
+  int M, H;
+  float eps;
+};
+cudaError_t launch_peer_allreduce_add_rms_norm(const PeerNormParams& p, cudaStream_t stream);
 
 // ------------------------------------------------------------------ direct
 // Direct kernel (gemv_direct.cuh): group-wise formats with one MMA step per

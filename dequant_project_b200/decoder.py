@@ -205,8 +205,9 @@ class TPDecoder:
     from disk) supplies them already packed, so no rank quantizes anything.
     Each rank takes its shard of every full matrix. ``allreduce`` picks the
     collective after the row-parallel layers on CUDA ranks: ``"peer"`` (the
-    GEMV, then the one-shot all-reduce over peer memory of ``peer_reduce``;
-    the default), ``"fused"`` (one kernel: the row-parallel GEMV exchanging
+    GEMV, then the one-shot all-reduce over peer memory of ``peer_reduce``,
+    run inside the residual add + RMSNorm that follows unless ``fuse_norm``
+    is False; the default), ``"fused"`` (one kernel: the row-parallel GEMV exchanging
     its partial rows through peer memory, where the shape has a fused plan) or
     ``"nccl"`` (``torch.distributed.all_reduce``); CPU ranks always use the
     process group. ``close()`` releases the peer mappings.
@@ -223,7 +224,7 @@ class TPDecoder:
                  group=None, device=None, seed: int = 0, batch: int = 1, kv_len: int = 2048,
                  max_new: int = 1, quantize_lm_head: bool = True,
                  linear_fn: Callable | None = None, weights=None, allreduce: str = "peer",
-                 l2_prefetch: bool = False):
+                 l2_prefetch: bool = False, fuse_norm: bool = True):
         if cfg.n_heads % world or cfg.n_kv_heads % world:
             raise ValueError(f"{cfg.n_heads} query / {cfg.n_kv_heads} KV heads do not split "
                              f"over {world} ranks")
@@ -306,6 +307,11 @@ class TPDecoder:
         self._peer = None
         self._pf = self._prefetch_spans() if l2_prefetch else None
         self._fused = allreduce == "fused"
+        # "peer": the all-reduce after a row-parallel layer runs inside the
+        # residual add + RMSNorm that follows it (one kernel instead of two).
+        self._norm_fused = (fuse_norm and allreduce == "peer" and world > 1
+                            and self.device.type == "cuda" and cfg.hidden % 8 == 0
+                            and cfg.hidden <= 8192 and not l2_prefetch)
         if world > 1 and allreduce != "nccl" and self.device.type == "cuda":
             from dequant_project_b200.peer_reduce import PeerAllReduce
             self._peer = PeerAllReduce(group, self.device, batch * cfg.hidden)
@@ -367,13 +373,24 @@ class TPDecoder:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
 
-    def _row_parallel(self, x: torch.Tensor, pw: PackedWeight) -> torch.Tensor:
-        """A row-parallel layer: the fused GEMV + peer all-reduce on CUDA ranks
-        with the peer collective (one kernel where the shape has a fused
-        plan), else this rank's GEMV and the all-reduce."""
+    def _row_parallel(self, x: torch.Tensor, pw: PackedWeight) -> tuple:
+        """A row-parallel layer: (output, reduced). With the fused GEMV +
+        peer all-reduce (``allreduce="fused"``) one kernel where the shape has
+        a fused plan; with the peer collective ("peer") this rank's partial
+        output, unreduced (``reduced`` False: the norm that follows reduces
+        it); otherwise this rank's GEMV and the all-reduce."""
         if self._peer is not None and self._fused and self._linear is _default_linear:
-            return self._peer.gemv(x, pw)
-        return self._all_reduce(self._linear(x, pw))
+            return self._peer.gemv(x, pw), True
+        if self._peer is not None and self._norm_fused:
+            return self._linear(x, pw), False
+        return self._all_reduce(self._linear(x, pw)), True
+
+    def _add_norm(self, h, delta, weight, reduced: bool, prefetch=None) -> torch.Tensor:
+        """Residual add + RMSNorm; a delta that is still a row-parallel
+        layer's unreduced partial is all-reduced by the same kernel."""
+        if delta is not None and not reduced:
+            return self._peer.add_rms_norm(delta, h, weight, self.cfg.eps)
+        return ops.add_rms_norm(h, delta, weight, self.cfg.eps, prefetch)
 
     def _lm_head(self, x: torch.Tensor) -> torch.Tensor:
         if isinstance(self.lm_head, PackedWeight):
@@ -398,21 +415,21 @@ class TPDecoder:
         h = self.embed[tokens]
         cos, sin = self.cos[pos], self.sin[pos]
         nq = self.hq * d
-        pending = None
+        pending, reduced = None, True
         for layer, w in enumerate(self.layers):
-            x = ops.add_rms_norm(h, pending, self.attn_norm[layer], cfg.eps,
-                                 self._prefetch(layer, "norm1"))
+            x = self._add_norm(h, pending, self.attn_norm[layer], reduced,
+                               self._prefetch(layer, "norm1"))
             qkv = self._linear(x, w["qkv"])
             kc, vc = self.k_cache[layer], self.v_cache[layer]
             q = ops.rope_kv_append(qkv, cos, sin, kc, vc, pos, self.hq, self.hkv,
                                    self._prefetch(layer, "rope"))
             a = ops.attention(q, kc, vc, pos + 1, self._attn_ws)
-            o = self._row_parallel(a.reshape(m, nq), w["o"])
-            x = ops.add_rms_norm(h, o, self.mlp_norm[layer], cfg.eps,
-                                 self._prefetch(layer, "norm2"))
+            o, o_reduced = self._row_parallel(a.reshape(m, nq), w["o"])
+            x = self._add_norm(h, o, self.mlp_norm[layer], o_reduced,
+                               self._prefetch(layer, "norm2"))
             act = ops.silu_mul(self._linear(x, w["gu"]), self._prefetch(layer, "silu"))
-            pending = self._row_parallel(act, w["down"])
-        x = ops.add_rms_norm(h, pending, self.final_norm, cfg.eps)
+            pending, reduced = self._row_parallel(act, w["down"])
+        x = self._add_norm(h, pending, self.final_norm, reduced)
         logits = self._lm_head(x)
         if self.world == 1:
             return logits

@@ -132,6 +132,30 @@ class PeerAllReduce:
             torch.cuda.current_stream(self.device).cuda_stream))
         return t
 
+    def add_rms_norm(self, partial: torch.Tensor, h: torch.Tensor, weight: torch.Tensor,
+                     eps: float) -> torch.Tensor:
+        """The all-reduce of ``partial`` [M, H] fused with the residual add +
+        RMSNorm after it (one kernel): ``h += sum over ranks of partial`` in
+        place and the returned fp16 ``RMSNorm(h) * weight``, the same bits as
+        this all-reduce followed by ``decode_ops.add_rms_norm``. ``partial`` is
+        left unchanged."""
+        if self._opened is None:
+            raise RuntimeError("peer all-reduce used after close()")
+        for t in (partial, h, weight):
+            if t.dtype != torch.float16 or not t.is_contiguous() or t.device != self.device:
+                raise RuntimeError("fused all-reduce + RMSNorm takes contiguous float16 tensors "
+                                   "on its device")
+        m, hd = h.shape
+        if tuple(partial.shape) != (m, hd) or weight.numel() != hd:
+            raise RuntimeError(f"shapes differ: partial {tuple(partial.shape)}, h {(m, hd)}, "
+                               f"weight {weight.numel()}")
+        y = torch.empty_like(h)
+        _native.check(_native.lib().dqg_peer_allreduce_add_rms_norm(
+            partial.data_ptr(), h.data_ptr(), weight.data_ptr(), y.data_ptr(), m, hd, float(eps),
+            self.peer_bufs, self.ctl.data_ptr(), self.cap, self.rank, self.world, self.wait_ns,
+            torch.cuda.current_stream(self.device).cuda_stream))
+        return y
+
     def gemv(self, x: torch.Tensor, pw) -> torch.Tensor:
         """Row-parallel layer: the sum over ranks of ``x_r @ W_r^T`` for this
         rank's slice ``x`` [M, K_r] and packed ``pw`` [N, K_r]; fp16 [M, N],

@@ -168,6 +168,25 @@ int dqg_peer_allreduce(const void *in, void *out, int64_t n, const uint64_t *pee
                        void *stream);
 
 /*
+ * The all-reduce of a row-parallel layer's output fused with the residual add
+ * + RMSNorm that follows it in the decoder step (no reference counterpart;
+ * the reference only models these bytes, dequant/byte_model.py:179-251):
+ * delta = the rank-order fp32 sum over ranks of `partial` [M, H] rounded to
+ * fp16, exactly as dqg_peer_allreduce gives it, then, exactly as
+ * dqg_add_rms_norm with that delta, h = fp16(h + delta) in place and
+ * y = fp16((h * rsqrt(mean(h^2) + eps)) * weight). Same receive buffers,
+ * call counters and rules as dqg_peer_allreduce (the two may be mixed in one
+ * sequence of calls); M * H <= cap, H a multiple of 8 up to 8192, all tensors
+ * fp16 and 16-byte aligned; partial is left unchanged. A row whose exchange
+ * ran out of time (bit 0 of dqg_device_status) leaves h and y unwritten.
+ * One launch instead of two, one CTA per row.
+ */
+int dqg_peer_allreduce_add_rms_norm(const void *partial, void *h, const void *weight, void *y,
+                                    int64_t M, int64_t H, float eps, const uint64_t *peer_bufs,
+                                    uint32_t *ctl, int64_t cap, int rank, int world,
+                                    uint64_t wait_ns, void *stream);
+
+/*
  * Row-parallel GEMV fused with its all-reduce: every rank passes its slice of
  * the input dimension (x [M, K_r], W_r [N, K_r] packed, as dqg_gemv) and gets
  * y = sum over ranks of x_r @ W_r^T, fp16 [M, N], the same bits on every rank.

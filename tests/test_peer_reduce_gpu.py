@@ -97,6 +97,64 @@ def test_missing_peer_gives_up_and_reports(cuda_device):
     assert _native.device_status(cuda_device.index) == 0
 
 
+def _norm_call(part, h, w, y, bufs, ctl, cap, rank, world, wait_ns=0, eps=1e-5):
+    ptrs = (ctypes.c_uint64 * world)(*[b.data_ptr() for b in bufs])
+    m, hd = h.shape
+    return _native.lib().dqg_peer_allreduce_add_rms_norm(
+        part.data_ptr(), h.data_ptr(), w.data_ptr(), y.data_ptr(), m, hd, eps, ptrs,
+        ctl.data_ptr(), cap, rank, world, wait_ns, torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("m,hd", [(1, 4096), (3, 1024), (2, 8192), (1, 8)])
+def test_fused_norm_gives_the_bits_of_allreduce_then_norm(cuda_device, m, hd):
+    """dqg_peer_allreduce_add_rms_norm with rank 1's packets in place: h and y
+    bit-identical to the all-reduced delta followed by dqg_add_rms_norm."""
+    from dequant_project_b200 import decode_ops
+    cap, world = 65536, 2
+    mine, peer = _buffers(cap, world, cuda_device), _buffers(cap, world, cuda_device)
+    ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    g = torch.Generator(device=cuda_device).manual_seed(m * hd)
+    a = torch.randn(m, hd, generator=g, device=cuda_device).half()
+    b = torch.randn(m, hd, generator=g, device=cuda_device).half()
+    h = (4 * torch.randn(m, hd, generator=g, device=cuda_device)).half()
+    w = (1 + 0.1 * torch.randn(hd, generator=g, device=cuda_device)).half()
+    n = m * hd
+    pk = _packets(mine, cap, world)
+    pk[1, 1, :n // 2, 0] = b.view(-1).view(torch.int32)
+    pk[1, 1, :n // 2, 1] = 1
+    h_ref = h.clone()
+    y_ref = decode_ops.add_rms_norm(h_ref, (a.float() + b.float()).half(), w, 1e-5)
+    y = torch.empty_like(h)
+    a0 = a.clone()
+    _native.device_status(cuda_device.index, reset=True)
+    _native.check(_norm_call(a, h, w, y, [mine, peer], ctl, cap, 0, world))
+    torch.cuda.synchronize()
+    assert torch.equal(h, h_ref) and torch.equal(y, y_ref)
+    assert torch.equal(a, a0)                      # the partial is left as it was
+    pp = _packets(peer, cap, world)
+    assert torch.equal(pp[1, 0, :n // 2, 0], a.view(-1).view(torch.int32))
+    assert ctl.tolist() == [1, 0] and _native.device_status(cuda_device.index) == 0
+
+
+def test_fused_norm_missing_peer_leaves_rows_alone(cuda_device):
+    cap, world, m, hd = 8192, 2, 2, 4096
+    mine, peer = _buffers(cap, world, cuda_device), _buffers(cap, world, cuda_device)
+    ctl = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    a = torch.randn(m, hd, device=cuda_device).half()
+    h = torch.randn(m, hd, device=cuda_device).half()
+    h0 = h.clone()
+    w = torch.ones(hd, dtype=torch.float16, device=cuda_device)
+    y = torch.full_like(h, 3.0)
+    _native.device_status(cuda_device.index, reset=True)
+    _native.check(_norm_call(a, h, w, y, [mine, peer], ctl, cap, 0, world, wait_ns=20_000_000))
+    torch.cuda.synchronize()
+    assert _native.device_status(cuda_device.index, reset=True) & 1
+    assert torch.equal(h, h0) and bool((y == 3.0).all())
+    assert ctl.tolist() == [1, 0]
+    bad = _norm_call(a, h, w, y, [mine, peer], ctl, 4096, 0, world)   # M * H > cap
+    assert bad == 1 and b"fit cap" in _native.lib().dqg_last_error()
+
+
 def test_rejects_bad_arguments(cuda_device):
     cap = 4096
     mine = _buffers(cap, 2, cuda_device)

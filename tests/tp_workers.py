@@ -210,8 +210,9 @@ def peer_allreduce_check(rank, world, port, queue):
 
 def decoder_peer_vs_nccl(rank, world, port, queue):
     """The small GPU test decoder on this NCCL rank with the peer all-reduce
-    and with NCCL's; both within 5e-3 of each other (the peer sum rounds once,
-    NCCL's fp16 sum per step). Reports the peer decoder's logits."""
+    (inside the following norm, and as its own kernel: the same bits) and with
+    NCCL's; within 5e-3 of each other (the peer sum rounds once, NCCL's fp16
+    sum per step). Reports the peer decoder's logits."""
     try:
         from dequant_project_b200.decoder import DecodeGraph, DecoderConfig, TPDecoder
         from dequant_project_b200.packer import QuantConfig
@@ -221,9 +222,10 @@ def decoder_peer_vs_nccl(rank, world, port, queue):
         dev = torch.device("cuda", rank)
         tokens = torch.tensor([3, 4001], device=dev)
         outs = {}
-        for mode in ("peer", "fused", "nccl"):
+        for mode in ("peer", "peer_unfused", "fused", "nccl"):
             dec = TPDecoder(cfg, QuantConfig(4, 128, False), world=world, rank=rank, device=dev,
-                            seed=5, batch=2, kv_len=100, allreduce=mode)
+                            seed=5, batch=2, kv_len=100, allreduce=mode.split("_")[0],
+                            fuse_norm=mode != "peer_unfused")
             eager = dec.step(tokens, 100).clone()
             gr = DecodeGraph(dec, 100)
             gr.tokens.copy_(tokens)
@@ -234,6 +236,9 @@ def decoder_peer_vs_nccl(rank, world, port, queue):
             if not torch.equal(rep, eager):
                 raise AssertionError(f"{mode}: graph replay differs from the eager step")
             outs[mode] = eager
+        # The all-reduce inside the norm kernel gives the bits of the two calls.
+        if not torch.equal(outs["peer"], outs["peer_unfused"]):
+            raise AssertionError("fused all-reduce + norm differs from the separate calls")
         b = outs["nccl"].float()
         for mode in ("peer", "fused"):
             a = outs[mode].float()
