@@ -14,6 +14,13 @@ cudaError_t launch_direct_b4(int wpl, int gs, bool sym, bool inter, const Direct
 cudaError_t launch_direct_b8(int wpl, int gs, bool sym, bool inter, const DirectParams& p,
                              int grid, int smem, cudaStream_t stream);
 
+#ifndef DQG_DIRECT_MAX_K
+#define DQG_DIRECT_MAX_K 6144
+#endif
+#ifndef DQG_DIRECT_MIN_BITS
+#define DQG_DIRECT_MIN_BITS 4
+#endif
+
 namespace {
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 }  // namespace
@@ -33,7 +40,7 @@ bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, Dir
   // takes batch 1 from 2.305 to 2.229 ms/token and batch 8 from 4.54 to 4.16;
   // on rows longer than 6144 codes and for 2-bit codes (4-byte copies per
   // lane) it is slower than the streaming kernel.
-  if (bits < 4 || K > 6144) return false;
+  if (bits < DQG_DIRECT_MIN_BITS || K > DQG_DIRECT_MAX_K) return false;
   (void)fused;
   int mp = 1;
   while (mp < M) mp <<= 1;
