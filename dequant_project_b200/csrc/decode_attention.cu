@@ -338,16 +338,40 @@ size_t attention_counter_bytes(int M, int Hkv) {
 #define DQG_ATTN_CTAS_PER_SM 2
 #endif
 
-int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out) {
-  const int mh = M * Hkv;
-  int s = (DQG_ATTN_CTAS_PER_SM * num_sms + mh - 1) / mh;
+namespace {
+// Splits of T positions when the target is `per_sm` CTAs per SM (positions
+// per split rounded up to whole tiles; *ts_out: positions per split).
+int splits_for(int mh, int T, int num_sms, int per_sm, int* ts_out) {
+  int s = (per_sm * num_sms + mh - 1) / mh;
   int max_s = (T + kTileT - 1) / kTileT;
   if (max_s > kMaxSplits) max_s = kMaxSplits;
   if (s > max_s) s = max_s;
   if (s < 1) s = 1;
   const int ts = ((T + s - 1) / s + kTileT - 1) / kTileT * kTileT;
-  if (ts_out) *ts_out = ts;
+  *ts_out = ts;
   return (T + ts - 1) / ts;
+}
+}  // namespace
+
+// Two CTAs fit on an SM. Of the splits that target one and two CTAs per SM,
+// take the one whose busiest SM streams fewer tiles (CTAs per SM, rounded up,
+// times tiles per CTA); on a tie the fewer splits (fewer CTAs, less merging).
+// Measured on B200: 7B heads at batch 1 keep two per SM (11.8 us; one per SM
+// leaves 12 SMs with two CTAs of 7 tiles, 12.8 us), batch 8 takes one split
+// per (sequence, head) (50.0 -> 43.9 us), the 16- and 8-head shards of
+// tensor-parallel ranks one per SM (9.7 -> 8.7 and 9.2 -> 7.8 us).
+int attention_splits(int M, int Hkv, int T, int num_sms, int* ts_out) {
+  const int mh = M * Hkv;
+  const int sms = num_sms > 0 ? num_sms : 1;
+  int ts1 = 0, ts2 = 0;
+  const int s1 = splits_for(mh, T, sms, 1, &ts1);
+  const int s2 = splits_for(mh, T, sms, DQG_ATTN_CTAS_PER_SM, &ts2);
+  const long long c1 = static_cast<long long>(mh) * s1, c2 = static_cast<long long>(mh) * s2;
+  const long long load1 = (c1 + sms - 1) / sms * ((ts1 + kTileT - 1) / kTileT);
+  const long long load2 = (c2 + sms - 1) / sms * ((ts2 + kTileT - 1) / kTileT);
+  const bool one = load1 <= load2;
+  if (ts_out) *ts_out = one ? ts1 : ts2;
+  return one ? s1 : s2;
 }
 
 size_t attention_workspace_bytes(int M, int Hq, int Hkv, int T, int num_sms) {
