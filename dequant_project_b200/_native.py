@@ -54,6 +54,10 @@ def lib() -> ctypes.CDLL:
     h.dqg_add_one.argtypes = [vp, vp, i64, vp]
     h.dqg_gemv.restype = i32
     h.dqg_gemv.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp]
+    h.dqg_gemv_swiglu.restype = i32
+    h.dqg_gemv_swiglu.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp]
+    h.dqg_gemv_swiglu_supported.restype = i32
+    h.dqg_gemv_swiglu_supported.argtypes = [i64, i64, i64, i64, i64, ctypes.POINTER(i32)]
     h.dqg_dequantize.restype = i32
     h.dqg_dequantize.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, vp]
     h.dqg_device_status.restype = i32
@@ -108,7 +112,8 @@ EXPORTED = ("dqg_last_error", "dqg_version", "dqg_add_one", "dqg_gemv", "dqg_deq
             "dqg_set_gemv_path", "dqg_decode_attention_workspace", "dqg_decode_attention",
             "dqg_gemv_allreduce", "dqg_decode_attention_noalloc",
             "dqg_ipc_export", "dqg_ipc_open", "dqg_ipc_close", "dqg_peer_allreduce",
-            "dqg_peer_allreduce_add_rms_norm")
+            "dqg_peer_allreduce_add_rms_norm", "dqg_gemv_swiglu",
+            "dqg_gemv_swiglu_supported")
 
 
 def check(rc: int) -> None:

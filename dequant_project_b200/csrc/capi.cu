@@ -337,6 +337,66 @@ int dqg_gemv(const void* x, const int32_t* qweight, const void* scales, const vo
   return ok();
 }
 
+int dqg_gemv_swiglu(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                    void* act, int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+                    int symmetric, int interleaved, void* stream) {
+  if (M < 1 || M > dqg::kMaxM)
+    return fail(DQG_ERR_INVALID, "gemv handles 1 <= M <= %d, got M=%lld", dqg::kMaxM,
+                (long long)M);
+  int rc = check_weight_args(qweight, scales, zeros, N, K, bits, group_size, symmetric);
+  if (rc) return rc;
+  if (N % 16 != 0)
+    return fail(DQG_ERR_INVALID, "N=%lld must be a multiple of 16 (8 gate rows, then 8 up rows)",
+                (long long)N);
+  if (x == nullptr || act == nullptr) return fail(DQG_ERR_INVALID, "x and act must not be null");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(qweight) % 16)
+    return fail(DQG_ERR_INVALID, "x and qweight must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(act) % 2) return fail(DQG_ERR_INVALID, "act must be 2-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  dqg::DirectPlan dplan;
+  if (!cached_direct_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                          static_cast<int>(bits), static_cast<int>(group_size), sm_count(dev),
+                          &dplan))
+    return fail(DQG_ERR_UNSUPPORTED, "no direct-kernel plan for this shape and format");
+  dqg::GemvArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.qweight = reinterpret_cast<const uint32_t*>(qweight);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.zeros = static_cast<const uint16_t*>(zeros);
+  a.y = static_cast<uint16_t*>(act);
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.bits = static_cast<int>(bits);
+  a.group_size = static_cast<int>(group_size);
+  a.symmetric = symmetric != 0;
+  a.interleaved = interleaved != 0;
+  e = dqg::launch_direct(a, dplan, static_cast<cudaStream_t>(stream), nullptr, true);
+  if (e != cudaSuccess) return cuda_fail(e, "gemv_swiglu launch");
+  return ok();
+}
+
+int dqg_gemv_swiglu_supported(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+                              int* supported) {
+  if (supported == nullptr) return fail(DQG_ERR_INVALID, "supported must not be null");
+  *supported = 0;
+  if (M < 1 || M > dqg::kMaxM || N < 16 || N % 16 != 0 || K < 1 || N > (1 << 30) ||
+      K > (1 << 30) || (bits != 2 && bits != 4 && bits != 8) || group_size <= 0)
+    return ok();
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  dqg::DirectPlan dplan;
+  *supported = cached_direct_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                  static_cast<int>(bits), static_cast<int>(group_size),
+                                  sm_count(dev), &dplan)
+                   ? 1
+                   : 0;
+  return ok();
+}
+
 int dqg_dequantize(const int32_t* qweight, const void* scales, const void* zeros, void* out,
                    int64_t N, int64_t K, int64_t bits, int64_t group_size, int symmetric,
                    int interleaved, void* stream) {

@@ -189,6 +189,10 @@ struct DirectParams {
   int xp;                 // bytes per permuted activation row in shared memory
   int off_x, off_sx, off_zero, off_red, off_tiles, off_ring;
   int prefetch;           // 1: first ring issued before the dependent-launch wait
+  // SwiGLU mode (N a multiple of 16, rows interleaved by 8: tile rows 0-7 the
+  // gate rows, 8-15 the up rows of the same outputs): y is [M, N / 2],
+  // y = silu(gate) * up.
+  int swiglu;
   // Row-parallel mode (ar_world > 1): y = the sum over ranks of every rank's
   // x_r @ W_r^T, exchanged through peer memory (see PeerGemvArgs).
   int ar_rank, ar_world;
@@ -219,7 +223,7 @@ struct DirectPlan {
 bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, DirectPlan* plan,
                  bool fused = false);
 cudaError_t launch_direct(const GemvArgs& args, const DirectPlan& plan, cudaStream_t stream,
-                          const PeerGemvArgs* ar = nullptr);
+                          const PeerGemvArgs* ar = nullptr, bool swiglu = false);
 
 // ------------------------------------------------------- decode attention
 struct AttnParams {

@@ -81,7 +81,7 @@ bool plan_direct(int M, int N, int K, int bits, int group_size, int num_sms, Dir
 }
 
 cudaError_t launch_direct(const GemvArgs& a, const DirectPlan& pl, cudaStream_t stream,
-                          const PeerGemvArgs* ar) {
+                          const PeerGemvArgs* ar, bool swiglu) {
   DirectParams p;
   p.x = a.x;
   p.qw = a.qweight;
@@ -101,6 +101,9 @@ cudaError_t launch_direct(const GemvArgs& a, const DirectPlan& pl, cudaStream_t 
   p.off_tiles = pl.off_tiles;
   p.off_ring = pl.off_ring;
   p.prefetch = weight_prefetch() ? 1 : 0;
+  p.swiglu = swiglu ? 1 : 0;
+  if (swiglu && (a.N % kTile != 0 || (ar != nullptr && ar->world > 1)))
+    return cudaErrorInvalidValue;
   p.ar_rank = 0;
   p.ar_world = 1;
   p.ar_ctl = nullptr;

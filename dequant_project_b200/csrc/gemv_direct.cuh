@@ -149,8 +149,16 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
   const int c = lane & 3;
   const int G = p.G;
   const int Gp = p.Gp;
-  const int row_begin = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
-  const int row_end = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
+  // Rows are balanced across CTAs to within one row; in SwiGLU mode to within
+  // one tile (a CTA's rows start on a tile, so that every tile pairs its gate
+  // rows 0-7 with its up rows 8-15).
+  const int row_begin =
+      p.swiglu ? static_cast<int>(static_cast<int64_t>(p.N / kTile) * blockIdx.x / gridDim.x) * kTile
+               : static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
+  const int row_end =
+      p.swiglu
+          ? static_cast<int>(static_cast<int64_t>(p.N / kTile) * (blockIdx.x + 1) / gridDim.x) * kTile
+          : static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
   const int T = (row_end - row_begin + kTile - 1) / kTile;
   // Warps split the CTA's steps evenly (to within one step): live steps are
   // [l_lo, l_hi). The loop runs over whole units around them, [s_lo, s_hi);
@@ -339,6 +347,16 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
   // Parity halves are a fixed cap apart, so that calls of different shapes
   // never write into the half a slower peer may still read.
   const int64_t ar_par = static_cast<int64_t>(ep & 1u) * p.ar_cap;
+  // SwiGLU mode: act[xrow, orow] from the gate and up sums, each rounded to
+  // fp16 as the GEMV's output is, then silu_mul_kernel's arithmetic
+  // (decode_ops.cu): fp16(g / (1 + exp(-g)) * u) in fp32.
+  auto store_swiglu = [&](int xrow, int orow, float gs, float us) {
+    const float g = __half2float(__float2half_rn(gs));
+    const float u = __half2float(__float2half_rn(us));
+    const float sg = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+    p.y[static_cast<int64_t>(xrow) * (p.N / 2) + orow] =
+        __half_as_ushort(__float2half_rn(__fmul_rn(sg, u)));
+  };
   auto store_out = [&](int xrow, int row, float v) {
     const int64_t e = static_cast<int64_t>(xrow) * p.N + row;
     if (ar)
@@ -445,7 +463,11 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
         const int xrow = (2 * c + (e & 1)) & (MP - 1);
         if (xrow < p.M) {
           if (whole) {
-            if (r0 + row < row_end) store_out(xrow, r0 + row, a[e]);
+            if (p.swiglu) {
+              if ((e >> 1) == 0) store_swiglu(xrow, (r0 >> 1) + gid, a[e], a[e + 2]);
+            } else if (r0 + row < row_end) {
+              store_out(xrow, r0 + row, a[e]);
+            }
           } else {
             rs[row * 8 + xrow] = a[e];
           }
@@ -553,8 +575,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
       if (w < warp) lowest = lowest && tl[2 * w] != t && tl[2 * w + 1] != t;
     if (!lowest) continue;
     const int r0 = row_begin + t * kTile;
-    for (int idx = lane; idx < kTile * p.M; idx += 32) {
-      const int row = idx / p.M, xrow = idx - (idx / p.M) * p.M;
+    auto tile_sum = [&](int row, int xrow) {
       float part[2 * kDirectNW];
 #pragma unroll
       for (int w = 0; w < kDirectNW; ++w) {
@@ -565,7 +586,19 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
       float sum = 0.f;
 #pragma unroll
       for (int i = 0; i < 2 * kDirectNW; ++i) sum += part[i];
-      if (r0 + row < row_end) store_out(xrow, r0 + row, sum);
+      return sum;
+    };
+    if (p.swiglu) {
+      for (int idx = lane; idx < (kTile / 2) * p.M; idx += 32) {
+        const int row = idx / p.M, xrow = idx - (idx / p.M) * p.M;
+        store_swiglu(xrow, (r0 >> 1) + row, tile_sum(row, xrow), tile_sum(row + 8, xrow));
+      }
+    } else {
+      for (int idx = lane; idx < kTile * p.M; idx += 32) {
+        const int row = idx / p.M, xrow = idx - (idx / p.M) * p.M;
+        const float sum = tile_sum(row, xrow);
+        if (r0 + row < row_end) store_out(xrow, r0 + row, sum);
+      }
     }
   }
   if (!ar) return;

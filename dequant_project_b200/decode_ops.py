@@ -107,6 +107,43 @@ def silu_mul(gate_up: torch.Tensor, prefetch=None) -> torch.Tensor:
     return out
 
 
+def gate_up_order(ir: int) -> torch.Tensor:
+    """Row order of a gate/up weight [2 ir, K] (gate rows, then up rows) for
+    ``gemv_swiglu``: blocks of 8 gate rows, each followed by the matching 8
+    up rows (ir a multiple of 8). Row j of the result is row order[j] of the
+    original."""
+    if ir % 8:
+        raise ValueError(f"the intermediate size {ir} is not a multiple of 8")
+    gate = torch.arange(ir // 8)[:, None] * 8 + torch.arange(8)[None, :]
+    return torch.cat([gate, gate + ir], dim=1).reshape(-1)
+
+
+def gemv_swiglu_supported(m: int, n: int, k: int, bits: int, group_size: int) -> bool:
+    """Whether ``gemv_swiglu`` has a kernel plan for [m] x [n, k] (CUDA)."""
+    import ctypes
+    v = ctypes.c_int(0)
+    _native.check(_native.lib().dqg_gemv_swiglu_supported(m, n, k, bits, group_size,
+                                                          ctypes.byref(v)))
+    return bool(v.value)
+
+
+def gemv_swiglu(x: torch.Tensor, pw) -> torch.Tensor:
+    """SwiGLU of the gate/up GEMV in one kernel: ``pw`` is a packed [2 I, K]
+    weight in ``gate_up_order``; returns fp16 [M, I] = silu(gate) * up, the
+    same values as ``silu_mul`` of the GEMV's de-interleaved output."""
+    from dequant_project_b200 import quant_linear as ql
+    n, k = pw.shape
+    x2 = x.reshape(-1, k).contiguous()
+    m = x2.shape[0]
+    bits, gs, sym, inter = ql._format_args(pw.config, k)
+    out = torch.empty((m, n // 2), dtype=torch.float16, device=x.device)
+    _native.check(_native.lib().dqg_gemv_swiglu(
+        x2.data_ptr(), pw.qweight.data_ptr(), pw.scales.data_ptr(),
+        None if pw.zeros is None else pw.zeros.data_ptr(), out.data_ptr(), m, n, k, bits, gs,
+        int(sym), int(inter), _stream(x2)))
+    return out
+
+
 def attention_workspace(m: int, n_q_heads: int, n_kv_heads: int, max_positions: int,
                         device) -> torch.Tensor:
     """Zeroed workspace for ``attention`` calls of up to ``max_positions``

@@ -309,6 +309,27 @@ int dqg_decode_attention_noalloc(const void *q, const void *k_cache, const void 
                                  int64_t head_dim, int64_t T, int64_t capacity, void *stream);
 
 /*
+ * The decoder's gate/up GEMV fused with its SwiGLU (no reference counterpart:
+ * the reference only models these bytes, dequant/byte_model.py:221-242). The
+ * packed weight [N, K] (format as dqg_gemv) holds the gate and up rows
+ * interleaved by eights: rows 16b .. 16b + 7 are gate rows 8b .. 8b + 7 and rows
+ * 16b + 8 .. 16b + 15 the matching up rows (N a multiple of 16).
+ * act[m, 8b + i] = fp16(silu(g) * u) with g and u the fp16-rounded GEMV
+ * outputs of those two rows, in dqg_silu_mul's arithmetic, so the result
+ * equals dqg_gemv on the interleaved weight followed by dqg_silu_mul on the
+ * de-interleaved halves. act is [M, N / 2]. One launch of the direct kernel;
+ * formats and shapes without a direct-kernel plan (4/8-bit group-wise
+ * formats whose group is one step, K up to 6144) return DQG_ERR_UNSUPPORTED.
+ */
+int dqg_gemv_swiglu(const void *x, const int32_t *qweight, const void *scales, const void *zeros,
+                    void *act, int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+                    int symmetric, int interleaved, void *stream);
+/* *supported = 1 when dqg_gemv_swiglu has a plan for this shape and format on
+ * the current device, else 0 (host only, no launch). */
+int dqg_gemv_swiglu_supported(int64_t M, int64_t N, int64_t K, int64_t bits, int64_t group_size,
+                              int *supported);
+
+/*
  * SwiGLU: gate_up is [M, 2 I] (gate columns, then up columns);
  * out[m, i] = fp16(silu(gate) * up), silu(g) = g / (1 + exp(-g)) in fp32.
  */

@@ -63,6 +63,8 @@ def reference_step(dec, tokens, pos, storage=None):
                 out[b, hh] = p @ vals
         h = rnd(h + linear(rnd(out).reshape(m, nq), w["o"]))
         gu = linear(norm(h), w["gu"])
+        if getattr(dec, "gu_order", None) is not None:   # rows stored interleaved by eights
+            gu = gu[:, torch.argsort(dec.gu_order.to(gu.device))]
         i = gu.shape[1] // 2
         act = rnd(torch.nn.functional.silu(gu[:, :i]) * gu[:, i:])
         h = rnd(h + linear(act, w["down"]))

@@ -122,6 +122,58 @@ def test_graph_replay_matches_eager():
     assert torch.equal(out, eager)
 
 
+@pytest.mark.parametrize("fmt", [(4, 128, False), (8, 64, True), (4, 64, False)])
+@pytest.mark.parametrize("m", [1, 2, 8])
+def test_gemv_swiglu_matches_gemv_then_silu(fmt, m):
+    """The gate/up GEMV fused with SwiGLU (rows interleaved by eights) against
+    the GEMV of the same interleaved weight, de-interleaved, then silu_mul."""
+    from dequant_project_b200 import dequant_cuda
+    from dequant_project_b200.packer import PackedWeight, quantize_tensor
+    bits, gs, sym = fmt
+    ir, k = 2816, 1024
+    g = torch.Generator(device="cuda").manual_seed(m * 31 + bits)
+    w = torch.randn(2 * ir, k, generator=g, device="cuda").half() * 0.05
+    pw = quantize_tensor(w, QuantConfig(bits, gs, sym))
+    order = decode_ops.gate_up_order(ir).cuda()
+    il = PackedWeight(pw.qweight[order].contiguous(), pw.scales[order].contiguous(),
+                      None if pw.zeros is None else pw.zeros[order].contiguous(), pw.config,
+                      pw.shape)
+    x = torch.randn(m, k, generator=g, device="cuda").half()
+    assert decode_ops.gemv_swiglu_supported(m, 2 * ir, k, bits, gs)
+    for _ in range(2):
+        act = decode_ops.gemv_swiglu(x, il)
+        y = dequant_cuda.gemv(x, il.qweight, il.scales, il.zeros, bits, gs, sym, False)
+        ref = decode_ops.silu_mul(y[:, torch.argsort(order)].contiguous())
+        assert act.shape == (m, ir)
+        torch.testing.assert_close(act.float(), ref.float(), rtol=2e-3,
+                                   atol=2e-3 * ref.float().abs().max().item())
+        assert (act == ref).float().mean().item() > 0.99   # most outputs bit-identical
+
+
+def test_gemv_swiglu_rejects_shapes_without_a_plan():
+    from dequant_project_b200 import _native
+    assert not decode_ops.gemv_swiglu_supported(1, 2 * 2816, 11008, 4, 128)   # K > 6144
+    assert not decode_ops.gemv_swiglu_supported(1, 2 * 2816, 4096, 2, 64)     # 2-bit codes
+    assert not decode_ops.gemv_swiglu_supported(1, 2 * 2816 + 8, 4096, 4, 128)   # N % 16
+    q = torch.zeros(16, 11008 // 8, dtype=torch.int32, device="cuda")
+    s = torch.ones(16, 86, dtype=torch.float16, device="cuda")
+    x = torch.zeros(1, 11008, dtype=torch.float16, device="cuda")
+    out = torch.empty(1, 8, dtype=torch.float16, device="cuda")
+    rc = _native.lib().dqg_gemv_swiglu(x.data_ptr(), q.data_ptr(), s.data_ptr(), None,
+                                       out.data_ptr(), 1, 16, 11008, 4, 128, 1, 0,
+                                       torch.cuda.current_stream().cuda_stream)
+    assert rc == 2 and b"no direct-kernel plan" in _native.lib().dqg_last_error()
+
+
+def test_decoder_swiglu_fusion_matches_separate_kernels():
+    q = QuantConfig(4, 128, False)
+    a = TPDecoder(SMALL, q, device="cuda", seed=8, batch=2, kv_len=64)
+    b = TPDecoder(SMALL, q, device="cuda", seed=8, batch=2, kv_len=64, fuse_swiglu=False)
+    assert a.gu_order is not None and b.gu_order is None
+    tokens = torch.tensor([5, 77], device="cuda")
+    assert max_rel_err(a.step(tokens, 64), b.step(tokens, 64).float()) < 2e-3
+
+
 def test_l2_prefetch_changes_nothing_but_timing():
     """The decoder with its element-wise ops prefetching later weights into
     L2 gives bit-identical logits, eager and graph-replayed, to the one
