@@ -223,10 +223,13 @@ def gemv_sweep(args, dev, peaks):
 
 
 def decode_launches(cfg, world: int) -> int:
-    """Launches of this library's kernels in one decode step: per layer two
-    norms, four GEMVs, RoPE + KV append, attention, SwiGLU (and two peer
-    all-reduces at world > 1); then the final norm and the LM head GEMV."""
-    return cfg.n_layers * (9 + (2 if world > 1 else 0)) + 2
+    """Launches of this library's kernels in one decode step of the default
+    decoder: per layer two norms (at world > 1 each with the all-reduce of the
+    row-parallel output before it inside), the QKV, O and down GEMVs, the
+    gate/up GEMV with its SwiGLU, RoPE + KV append and attention; then the
+    final norm and the LM head GEMV. ``world`` does not change the count."""
+    del world
+    return cfg.n_layers * 8 + 2
 
 
 def run_ours(args, rank, world, local_rank):
