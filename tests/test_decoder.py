@@ -215,3 +215,18 @@ def test_generate_is_greedy_stepping():
     assert torch.equal(ids, torch.stack(want, dim=1))
     with pytest.raises(ValueError, match="exceed the cache"):
         dec.generate(torch.tensor([3, 400]), 5)
+
+
+def test_gate_up_order_interleaves_by_eights():
+    """The row order of the fused gate/up + SwiGLU kernel: 8 gate rows, then
+    the same outputs' 8 up rows; a permutation that argsort undoes."""
+    from dequant_project_b200 import decode_ops
+    ir = 24
+    order = decode_ops.gate_up_order(ir)
+    assert order.tolist()[:16] == list(range(8)) + list(range(ir, ir + 8))
+    assert order.tolist()[16:32] == list(range(8, 16)) + list(range(ir + 8, ir + 16))
+    assert sorted(order.tolist()) == list(range(2 * ir))
+    y = torch.arange(2 * ir, dtype=torch.float32)[None, :]
+    assert torch.equal(y[:, order][:, torch.argsort(order)], y)
+    with pytest.raises(ValueError):
+        decode_ops.gate_up_order(12)
